@@ -1,0 +1,239 @@
+/*
+ * purin_cp.h -- C ABI of the B200 Chambolle--Pock projection layer.
+ *
+ * This library replaces the numerical core of PURIN's CP projection path
+ * (SOULS-TAMU/Purin 1.0.2).  The reference runs that core as two jitted JAX
+ * custom-VJP functions; a host binding (torch, ctypes, or a jax.ffi adapter)
+ * calls the entry points below in their place:
+ *
+ *   purin_cp_plan_create  <- PreparedChambollePockProjection.__post_init__
+ *                            (src/purin/solvers/chambolle_pock/solver.py:32-65):
+ *                            padded-ELL layout (kernels.py:26-40) and the bound
+ *                            presolve row selection (bounds.py:320-326).
+ *   purin_cp_forward      <- BoundProjection.solve_jit forward
+ *                            (bounds.py:42-66, called at bounds.py:237-246) and
+ *                            _solve_jit forward (solver.py:149-176, called at
+ *                            solver.py:332): sparse_cp (kernels.py:178-305).
+ *   purin_cp_adjoint      <- the custom-VJP backward (bounds.py:80-165;
+ *                            solver.py:186-272): power-iteration step sizes,
+ *                            restarted GMRES (primal_dual_interior_point/
+ *                            operators.py:792-1125) on the CP fixed-point
+ *                            adjoint, and the parameter pullback.
+ *   purin_cp_postprocess  <- BoundProjection.solve post-processing
+ *                            (bounds.py:247-317; solver.py:333-366): multiplier
+ *                            recovery in original units, residuals, status.
+ *
+ * Conventions.  All array arguments are DEVICE pointers on the plan's device,
+ * row-major, batch-major ((B, n) means B rows of n).  Floating arrays use the
+ * plan's dtype (double or float).  Boolean arrays are uint8 (0/1).  Nothing
+ * here allocates, synchronises the host, or calls cudaDeviceSynchronize; all
+ * work is enqueued on the caller's stream (a cudaStream_t passed as void*).
+ * The caller owns every buffer, including the workspace whose size
+ * purin_cp_workspace_size reports.  A plan is immutable after creation and can
+ * be used from several host threads on different streams, each call with its
+ * own workspace.
+ *
+ * Errors.  Every function returns a PurinStatus; on failure
+ * purin_cp_last_error() returns a thread-local message.  Numerical failures
+ * (non-convergence, non-finite iterates) are not errors: they are reported per
+ * sample through converged / status arrays, as in the reference.
+ */
+#ifndef PURIN_CP_H
+#define PURIN_CP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PURIN_CP_ABI_VERSION 1
+
+typedef enum PurinStatus {
+  PURIN_OK = 0,
+  PURIN_ERR_INVALID_ARGUMENT = 1,
+  PURIN_ERR_UNSUPPORTED = 2,
+  PURIN_ERR_CUDA = 3,
+  PURIN_ERR_WORKSPACE = 4
+} PurinStatus;
+
+typedef enum PurinDtype { PURIN_FLOAT64 = 0, PURIN_FLOAT32 = 1 } PurinDtype;
+
+/* Which computation a workspace is sized for. */
+typedef enum PurinCpOp {
+  PURIN_CP_OP_FORWARD = 0,
+  PURIN_CP_OP_ADJOINT = 1
+} PurinCpOp;
+
+/* Index arrays derived by the plan (purin_cp_plan_indices). */
+typedef enum PurinCpIndex {
+  PURIN_CP_KEPT_ROWS = 0,       /* m_kept: original row of each kept row            */
+  PURIN_CP_KEPT_SLOTS = 1,      /* nnz_kept: original CSR slot of each kept slot    */
+  PURIN_CP_BOUND_ROWS = 2,      /* n_bound: original row of each bound row          */
+  PURIN_CP_BOUND_SLOTS = 3,     /* n_bound: CSR slot of each bound row's coefficient */
+  PURIN_CP_BOUND_VARIABLES = 4, /* n_bound: variable each bound row constrains      */
+  PURIN_CP_KEPT_ROW_PTR = 5,    /* m_kept+1: CSR row pointer of the kept rows        */
+  PURIN_CP_KEPT_COLS = 6        /* nnz_kept: column of each kept slot                */
+} PurinCpIndex;
+
+typedef struct PurinCpPlan PurinCpPlan;
+
+/* Static sparsity of the public constraint rows: equality rows first, then
+ * inequality rows, each row's columns in the order of the problem's sparsity
+ * tuples (PreparedChambollePockProjection.__post_init__, solver.py:44-52). */
+typedef struct PurinCpStructure {
+  int32_t n;               /* variables                                 */
+  int32_t equality_size;   /* me                                        */
+  int32_t inequality_size; /* mi (all public inequality rows)           */
+  const int32_t* row_ptr;  /* HOST pointer, me+mi+1 entries             */
+  const int32_t* col;      /* HOST pointer, row_ptr[me+mi] entries      */
+  int32_t dtype;           /* PurinDtype                                */
+  int32_t device;          /* CUDA device ordinal                       */
+} PurinCpStructure;
+
+typedef struct PurinCpPlanInfo {
+  int32_t n;
+  int32_t equality_size;
+  int32_t inequality_size;
+  int32_t kept_rows;   /* m = me + kept inequality rows (CP rows)       */
+  int32_t kept_nnz;    /* nonzeros of the kept rows                     */
+  int32_t bound_rows;  /* singleton inequality rows turned into bounds  */
+  int32_t nnz;         /* nonzeros of all public rows                   */
+  int32_t width;       /* padded row width of the reference layout      */
+  int32_t dtype;
+  int32_t device;
+} PurinCpPlanInfo;
+
+/* Field-for-field ChambollePockConfig (chambolle_pock/config.py:34-48) for the
+ * fields the CP kernels read; tolerance arrives per sample in the call. */
+typedef struct PurinCpConfig {
+  int32_t max_iterations;
+  int32_t accelerated;
+  double safety;
+  int32_t norm_iterations;
+  int64_t norm_seed;
+  int32_t norm_bound;
+  int32_t diagonal_preconditioning;
+  int32_t prng_partitionable; /* 1: jax_threefry_partitionable key scheme (JAX >= 0.5) */
+} PurinCpConfig;
+
+/* LinearSolverConfig (solvers/config.py:10-25) + ImplicitGradientConfig
+ * .adjoint_tolerance (solvers/config.py:28-44). */
+typedef struct PurinLinearSolverConfig {
+  double tolerance;
+  double atol;
+  int32_t restart;
+  int32_t max_iterations;
+  double adjoint_tolerance;
+} PurinLinearSolverConfig;
+
+/* purin_cp_forward: the arguments of BoundProjection.solve_jit
+ * (bounds.py:237-246) and the CPOutput fields it returns (kernels.py:15-23),
+ * plus `converged &= feasible` (bounds.py:66).  m = kept rows. */
+typedef struct PurinCpForwardArgs {
+  int64_t batch;
+  const void* values;       /* scaled kept-row values, kept CSR slot order   */
+  int64_t values_stride;    /* 0 (shared by the batch) or kept_nnz           */
+  const void* rhs;          /* (B, m) scaled kept right-hand sides           */
+  const void* target;       /* (B, n) projection targets (also y0)           */
+  const void* dual0;        /* (B, m) warm-start duals, or NULL for zeros    */
+  const void* tolerance;    /* (B,) per-sample solve tolerance               */
+  const void* lower;        /* (B, n) or (n,) lower bounds (-inf allowed)    */
+  const void* upper;        /* (B, n) or (n,) upper bounds (+inf allowed)    */
+  int64_t bounds_stride;    /* 0 (shared) or n                               */
+  const uint8_t* feasible;  /* (B,) presolve feasibility, or NULL (all ok)   */
+  int64_t sample_offset;    /* index of sample 0 in the global batch (PRNG)  */
+  int64_t total_batch;      /* global batch size (PRNG key split count)      */
+  void* y;                  /* out (B, n)                                    */
+  void* dual;               /* out (B, m)                                    */
+  int32_t* iterations;      /* out (B,)                                      */
+  void* residual;           /* out (B,)                                      */
+  void* gap;                /* out (B,)                                      */
+  uint8_t* converged;       /* out (B,)                                      */
+} PurinCpForwardArgs;
+
+/* purin_cp_adjoint: the saved residuals of bounds.py:78 and the cotangent of
+ * y; returns the cotangents of (values, rhs, target, lower, upper) as
+ * bounds.py:156-165 does.  Output pointers may be NULL to skip an output. */
+typedef struct PurinCpAdjointArgs {
+  int64_t batch;
+  const void* values;       /* scaled kept-row values (as in the forward)    */
+  int64_t values_stride;
+  const void* rhs;          /* (B, m)                                        */
+  const void* target;       /* (B, n)                                        */
+  const void* lower;        /* (B, n) or (n,)                                */
+  const void* upper;
+  int64_t bounds_stride;
+  const void* y;            /* (B, n) forward solution                       */
+  const void* dual;         /* (B, m) forward duals                          */
+  const uint8_t* converged; /* (B,) forward convergence (after feasibility)  */
+  const void* cot_y;        /* (B, n) cotangent of y                         */
+  int64_t sample_offset;
+  int64_t total_batch;
+  void* grad_values;        /* out (B, kept_nnz) per-sample, or NULL         */
+  void* grad_rhs;           /* out (B, m) or NULL                            */
+  void* grad_target;        /* out (B, n) or NULL                            */
+  void* grad_lower;         /* out (B, n) or NULL                            */
+  void* grad_upper;         /* out (B, n) or NULL                            */
+  int32_t* linear_status;   /* out (B,) GMRES info 0/1/2, or NULL            */
+  void* linear_residual;    /* out (B,) GMRES residual inf-norm, or NULL     */
+  int32_t* device_error;    /* out (1,) 0, or nonzero when a bounded device
+                               wait gave up (outputs are then unspecified)   */
+} PurinCpAdjointArgs;
+
+/* purin_cp_postprocess: bounds.py:247-305 on the unscaled public rows. */
+typedef struct PurinCpPostArgs {
+  int64_t batch;
+  const void* values_all;   /* unscaled public-row values, CSR slot order    */
+  int64_t values_all_stride;/* 0 or nnz                                      */
+  const void* rhs_all;      /* (B, me+mi)                                    */
+  const void* target;       /* (B, n)                                        */
+  const void* lower;        /* (B, n) or (n,) presolve bounds                */
+  const void* upper;
+  int64_t bounds_stride;
+  const void* scale;        /* (B, m) kept-row scaling                       */
+  const void* y;            /* (B, n) forward solution                       */
+  const void* dual;         /* (B, m) forward (scaled) duals                 */
+  const void* gap;          /* (B,) forward gap                              */
+  const uint8_t* cp_converged; /* (B,) forward convergence                   */
+  double tolerance;         /* ChambollePockConfig.tolerance                 */
+  void* multipliers_eq;     /* out (B, me)                                   */
+  void* multipliers_ineq;   /* out (B, mi)                                   */
+  void* slacks;             /* out (B, mi)                                   */
+  int32_t* status;          /* out (B,) SolveStatus                          */
+  void* residual_inf_norm;  /* out (B,)                                      */
+  uint8_t* finite;          /* out (B,)                                      */
+  uint8_t* gradient_eligible; /* out (B,)                                    */
+} PurinCpPostArgs;
+
+int32_t purin_cp_abi_version(void);
+const char* purin_cp_last_error(void);
+
+int32_t purin_cp_plan_create(const PurinCpStructure* structure, PurinCpPlan** plan);
+int32_t purin_cp_plan_destroy(PurinCpPlan* plan);
+int32_t purin_cp_plan_info(const PurinCpPlan* plan, PurinCpPlanInfo* info);
+/* Copies the requested index array into HOST memory `out` (size per enum). */
+int32_t purin_cp_plan_indices(const PurinCpPlan* plan, int32_t which, int32_t* out);
+
+int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t batch,
+                                const PurinCpConfig* config,
+                                const PurinLinearSolverConfig* linear, size_t* bytes);
+
+int32_t purin_cp_forward(const PurinCpPlan* plan, const PurinCpConfig* config,
+                         const PurinCpForwardArgs* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config,
+                         const PurinLinearSolverConfig* linear,
+                         const PurinCpAdjointArgs* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PURIN_CP_H */

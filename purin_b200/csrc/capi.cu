@@ -1,0 +1,595 @@
+// C ABI of the CP projection library (declared in include/purin_cp.h).
+//
+// Host-side runtime: plan construction (the prepare step of
+// PreparedChambollePockProjection, solver.py:32-65, and prepare_bounds,
+// bounds.py:320-326), argument validation, workspace layout, tile planning
+// and kernel dispatch.  Nothing here allocates during a solve: the plan owns
+// only the immutable index arrays, the caller owns every per-call buffer.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/purin_cp.h"
+#include "cp_kernels.cuh"
+#include "plan.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* where) {
+  return fail(PURIN_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int previous = -1;
+  bool ok = false;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
+    ok = cudaSetDevice(device) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (previous >= 0) cudaSetDevice(previous);
+  }
+};
+
+size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t dtype_size(int32_t dtype) { return dtype == PURIN_FLOAT64 ? 8 : 4; }
+
+constexpr uint64_t kBarrierTimeoutNs = 60ull * 1000ull * 1000ull * 1000ull;
+
+// Forward tile plan: samples per CTA and whether the tile state fits in shared memory.
+struct FwdPlan {
+  int S = 1;
+  bool smem = true;
+  size_t smem_bytes = 0;
+  size_t workspace = 0;
+};
+
+FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
+  FwdPlan fp;
+  const int n = plan->info.n, m = plan->info.kept_rows;
+  const size_t w = dtype_size(plan->info.dtype);
+  const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
+  const size_t per_sample = (size_t)(2 * n + m + (diag ? 2 * n + m : 0)) * w;
+  const size_t cap = (size_t)plan->max_smem_optin;
+  const int64_t target_tiles = 2 * (int64_t)std::max(1, plan->sm_count);
+  int best = 0;
+  for (int S = 1; S <= 32; S *= 2) {
+    const size_t stat = plan->info.dtype == PURIN_FLOAT64 ? purin::forward_static_smem<double>(S)
+                                                          : purin::forward_static_smem<float>(S);
+    if ((size_t)S * per_sample + stat + 1024 > cap) break;
+    const int64_t tiles = (batch + S - 1) / S;
+    if (S == 1 || tiles >= target_tiles) best = S;
+  }
+  if (best > 0) {
+    fp.S = best;
+    fp.smem = true;
+    fp.smem_bytes = (size_t)best * per_sample;
+    fp.workspace = 0;
+  } else {
+    fp.S = 8;
+    fp.smem = false;
+    fp.smem_bytes = 0;
+    const int64_t tiles = (batch + fp.S - 1) / fp.S;
+    fp.workspace = align_up((size_t)tiles * fp.S * per_sample);
+  }
+  return fp;
+}
+
+struct AdjLayout {
+  int R = 1;
+  int grid = 0;
+  bool smem = true;
+  size_t off_x, off_lamp, off_steps, off_dsteps, off_thresh, off_resinf, off_basis, off_gbuf;
+  size_t off_ycode, off_dcode, off_counters, counters_bytes, total;
+};
+
+AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
+                       const PurinLinearSolverConfig* lin, int64_t batch) {
+  AdjLayout L;
+  const int n = plan->info.n, m = plan->info.kept_rows;
+  const int64_t W = 2 * (int64_t)n + m;
+  const size_t w = dtype_size(plan->info.dtype);
+  L.R = (int)std::min<int64_t>(std::min<int64_t>(lin->restart, lin->max_iterations), W);
+  if (L.R < 1) L.R = 1;
+  const bool f64 = plan->info.dtype == PURIN_FLOAT64;
+  const size_t smem_full = f64 ? purin::adjoint_smem_bytes<double>(n, m, L.R, true)
+                               : purin::adjoint_smem_bytes<float>(n, m, L.R, true);
+  L.smem = smem_full + 1024 <= (size_t)plan->max_smem_optin;
+  L.grid = f64 ? purin::adjoint_grid<double>(plan->sm_count, n, m, L.R, L.smem, batch)
+               : purin::adjoint_grid<float>(plan->sm_count, n, m, L.R, L.smem, batch);
+  const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes);
+    return o;
+  };
+  L.off_x = take((size_t)batch * W * w);
+  L.off_lamp = take((size_t)batch * m * w);
+  L.off_steps = take((size_t)batch * 2 * w);
+  L.off_dsteps = take(diag ? (size_t)batch * (2 * n + m) * w : 0);
+  L.off_thresh = take((size_t)batch * w);
+  L.off_resinf = take((size_t)batch * w);
+  L.off_basis = take((size_t)std::max(L.grid, 1) * (L.R + 1) * W * w);
+  L.off_gbuf = take(L.smem ? 0 : (size_t)std::max(L.grid, 1) * (W + n + m) * w);
+  L.off_ycode = take((size_t)batch * n);
+  L.off_dcode = take((size_t)batch * m);
+  L.counters_bytes = align_up(2 * (size_t)(lin->max_iterations + 2) * sizeof(unsigned) +
+                              sizeof(purin::GridBarrier));
+  L.off_counters = take(L.counters_bytes);
+  L.total = off;
+  return L;
+}
+
+int32_t check_plan(const PurinCpPlan* plan) {
+  if (!plan) return fail(PURIN_ERR_INVALID_ARGUMENT, "plan is NULL");
+  return PURIN_OK;
+}
+
+int32_t check_config(const PurinCpConfig* cfg) {
+  if (!cfg) return fail(PURIN_ERR_INVALID_ARGUMENT, "config is NULL");
+  if (cfg->max_iterations < 1) return fail(PURIN_ERR_INVALID_ARGUMENT, "max_iterations must be a positive integer");
+  if (!(cfg->safety > 0.0 && cfg->safety < 1.0))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "safety must be between zero and one");
+  if (cfg->norm_iterations < 1) return fail(PURIN_ERR_INVALID_ARGUMENT, "norm_iterations must be a positive integer");
+  return PURIN_OK;
+}
+
+int32_t check_linear(const PurinLinearSolverConfig* lin) {
+  if (!lin) return fail(PURIN_ERR_INVALID_ARGUMENT, "linear solver config is NULL");
+  if (!(lin->tolerance > 0.0) || lin->atol < 0.0) return fail(PURIN_ERR_INVALID_ARGUMENT, "linear tolerances are invalid");
+  if (lin->restart < 1 || lin->max_iterations < 1)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "linear iteration limits must be positive");
+  return PURIN_OK;
+}
+
+template <typename T>
+int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinCpForwardArgs* a,
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const FwdPlan fp = plan_forward(plan, cfg, a->batch);
+  if (!fp.smem && (workspace == nullptr || workspace_bytes < fp.workspace))
+    return fail(PURIN_ERR_WORKSPACE, "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes");
+  purin::FwdParams<T> p{};
+  p.st = plan->dev;
+  p.batch = a->batch;
+  p.values = static_cast<const T*>(a->values);
+  p.values_stride = a->values_stride;
+  p.rhs = static_cast<const T*>(a->rhs);
+  p.target = static_cast<const T*>(a->target);
+  p.dual0 = static_cast<const T*>(a->dual0);
+  p.tol = static_cast<const T*>(a->tolerance);
+  p.lower = static_cast<const T*>(a->lower);
+  p.upper = static_cast<const T*>(a->upper);
+  p.bounds_stride = a->bounds_stride;
+  p.feasible = a->feasible;
+  p.sample_offset = a->sample_offset;
+  p.total_batch = a->total_batch > 0 ? a->total_batch : a->batch;
+  p.y_out = static_cast<T*>(a->y);
+  p.dual_out = static_cast<T*>(a->dual);
+  p.it_out = a->iterations;
+  p.res_out = static_cast<T*>(a->residual);
+  p.gap_out = static_cast<T*>(a->gap);
+  p.conv_out = a->converged;
+  p.max_iterations = cfg->max_iterations;
+  p.accelerated = cfg->accelerated ? 1 : 0;
+  p.safety = (T)cfg->safety;
+  p.norm_iterations = cfg->norm_iterations;
+  p.norm_seed = cfg->norm_seed;
+  p.norm_bound = cfg->norm_bound ? 1 : 0;
+  p.diag = (cfg->diagonal_preconditioning && !cfg->accelerated) ? 1 : 0;
+  p.partitionable = cfg->prng_partitionable ? 1 : 0;
+  p.gstate = fp.smem ? nullptr : static_cast<T*>(workspace);
+  cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.smem, fp.smem_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward launch");
+  return PURIN_OK;
+}
+
+template <typename T>
+int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
+                    const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
+  if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
+  if (!a->device_error) return fail(PURIN_ERR_INVALID_ARGUMENT, "device_error pointer is required");
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws + L.off_counters, 0, L.counters_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
+  e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
+  purin::AdjParams<T> p{};
+  p.st = plan->dev;
+  p.batch = a->batch;
+  p.values = static_cast<const T*>(a->values);
+  p.values_stride = a->values_stride;
+  p.rhs = static_cast<const T*>(a->rhs);
+  p.target = static_cast<const T*>(a->target);
+  p.lower = static_cast<const T*>(a->lower);
+  p.upper = static_cast<const T*>(a->upper);
+  p.bounds_stride = a->bounds_stride;
+  p.y = static_cast<const T*>(a->y);
+  p.dual = static_cast<const T*>(a->dual);
+  p.converged = a->converged;
+  p.cot_y = static_cast<const T*>(a->cot_y);
+  p.sample_offset = a->sample_offset;
+  p.total_batch = a->total_batch > 0 ? a->total_batch : a->batch;
+  p.g_values = static_cast<T*>(a->grad_values);
+  p.g_rhs = static_cast<T*>(a->grad_rhs);
+  p.g_target = static_cast<T*>(a->grad_target);
+  p.g_lower = static_cast<T*>(a->grad_lower);
+  p.g_upper = static_cast<T*>(a->grad_upper);
+  p.lin_status = a->linear_status;
+  p.lin_residual = static_cast<T*>(a->linear_residual);
+  p.device_error = a->device_error;
+  p.accelerated = cfg->accelerated ? 1 : 0;
+  p.diag = (cfg->diagonal_preconditioning && !cfg->accelerated) ? 1 : 0;
+  p.norm_iterations = cfg->norm_iterations;
+  p.partitionable = cfg->prng_partitionable ? 1 : 0;
+  p.norm_seed = cfg->norm_seed;
+  p.safety = (T)cfg->safety;
+  p.lin_tol = (T)lin->tolerance;
+  p.lin_atol = (T)lin->atol;
+  p.adj_tol = (T)lin->adjoint_tolerance;
+  p.R = L.R;
+  p.max_it = lin->max_iterations;
+  p.timeout_ns = kBarrierTimeoutNs;
+  p.x = reinterpret_cast<T*>(ws + L.off_x);
+  p.lamp = reinterpret_cast<T*>(ws + L.off_lamp);
+  p.steps = reinterpret_cast<T*>(ws + L.off_steps);
+  p.dsteps = reinterpret_cast<T*>(ws + L.off_dsteps);
+  p.thresh = reinterpret_cast<T*>(ws + L.off_thresh);
+  p.resinf = reinterpret_cast<T*>(ws + L.off_resinf);
+  p.basis = reinterpret_cast<T*>(ws + L.off_basis);
+  p.gbuf = L.smem ? nullptr : reinterpret_cast<T*>(ws + L.off_gbuf);
+  p.ycode = reinterpret_cast<uint8_t*>(ws + L.off_ycode);
+  p.dcode = reinterpret_cast<uint8_t*>(ws + L.off_dcode);
+  unsigned* counters = reinterpret_cast<unsigned*>(ws + L.off_counters);
+  p.cycle_len = counters;
+  p.cycle_act = counters + (lin->max_iterations + 2);
+  p.barrier = reinterpret_cast<purin::GridBarrier*>(counters + 2 * (lin->max_iterations + 2));
+  e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch");
+  return PURIN_OK;
+}
+
+template <typename T>
+int32_t run_post(const PurinCpPlan* plan, const PurinCpPostArgs* a, cudaStream_t stream) {
+  purin::PostParams<T> p{};
+  p.st = plan->dev;
+  p.batch = a->batch;
+  p.values_all = static_cast<const T*>(a->values_all);
+  p.values_stride = a->values_all_stride;
+  p.rhs_all = static_cast<const T*>(a->rhs_all);
+  p.target = static_cast<const T*>(a->target);
+  p.lower = static_cast<const T*>(a->lower);
+  p.upper = static_cast<const T*>(a->upper);
+  p.bounds_stride = a->bounds_stride;
+  p.scale = static_cast<const T*>(a->scale);
+  p.y = static_cast<const T*>(a->y);
+  p.dual = static_cast<const T*>(a->dual);
+  p.gap = static_cast<const T*>(a->gap);
+  p.cp_conv = a->cp_converged;
+  p.tol = (T)a->tolerance;
+  p.meq = static_cast<T*>(a->multipliers_eq);
+  p.miq = static_cast<T*>(a->multipliers_ineq);
+  p.slacks = static_cast<T*>(a->slacks);
+  p.status = a->status;
+  p.resid = static_cast<T*>(a->residual_inf_norm);
+  p.finite = a->finite;
+  p.elig = a->gradient_eligible;
+  cudaError_t e = purin::launch_post<T>(p, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_postprocess launch");
+  return PURIN_OK;
+}
+
+// Counting sort of (row, slot) entries by column, stable in row-major order.
+void build_csc(int n, const std::vector<int32_t>& row_ptr, const std::vector<int32_t>& col,
+               std::vector<int32_t>& col_ptr, std::vector<int32_t>& csc_row,
+               std::vector<int32_t>& csc_slot) {
+  const int m = (int)row_ptr.size() - 1;
+  const int nnz = row_ptr.back();
+  col_ptr.assign(n + 1, 0);
+  for (int k = 0; k < nnz; ++k) col_ptr[col[k] + 1]++;
+  for (int j = 0; j < n; ++j) col_ptr[j + 1] += col_ptr[j];
+  std::vector<int32_t> fill(col_ptr.begin(), col_ptr.end() - 1);
+  csc_row.assign(nnz, 0);
+  csc_slot.assign(nnz, 0);
+  for (int i = 0; i < m; ++i) {
+    for (int k = row_ptr[i]; k < row_ptr[i + 1]; ++k) {
+      const int q = fill[col[k]]++;
+      csc_row[q] = i;
+      csc_slot[q] = k;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t purin_cp_abi_version(void) { return PURIN_CP_ABI_VERSION; }
+
+const char* purin_cp_last_error(void) { return g_last_error.c_str(); }
+
+int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
+  if (!s || !out) return fail(PURIN_ERR_INVALID_ARGUMENT, "structure and output pointers are required");
+  *out = nullptr;
+  const int n = s->n, me = s->equality_size, mi = s->inequality_size;
+  if (n < 1) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch_size and variable_size must be positive");
+  if (me < 0 || mi < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "constraint row counts must be nonnegative");
+  if (s->dtype != PURIN_FLOAT64 && s->dtype != PURIN_FLOAT32)
+    return fail(PURIN_ERR_UNSUPPORTED, "dtype must be float64 or float32");
+  const int m_all = me + mi;
+  if (m_all > 0 && (!s->row_ptr || (s->row_ptr[m_all] > 0 && !s->col)))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "row_ptr/col are required");
+  std::vector<int32_t> row_ptr(m_all + 1, 0), col;
+  if (m_all > 0) {
+    if (s->row_ptr[0] != 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "row_ptr[0] must be 0");
+    for (int i = 0; i < m_all; ++i) {
+      if (s->row_ptr[i + 1] < s->row_ptr[i]) return fail(PURIN_ERR_INVALID_ARGUMENT, "row_ptr must be nondecreasing");
+      row_ptr[i + 1] = s->row_ptr[i + 1];
+    }
+    col.assign(s->col, s->col + row_ptr[m_all]);
+    for (int32_t c : col)
+      if (c < 0 || c >= n) return fail(PURIN_ERR_INVALID_ARGUMENT, "column index out of range");
+  }
+  int device_count = 0;
+  if (cudaGetDeviceCount(&device_count) != cudaSuccess || s->device < 0 || s->device >= device_count)
+    return fail(PURIN_ERR_CUDA, "CUDA device " + std::to_string(s->device) + " is not available");
+
+  auto* plan = new PurinCpPlan();
+  PurinCpPlanInfo& info = plan->info;
+  info.n = n;
+  info.equality_size = me;
+  info.inequality_size = mi;
+  info.nnz = row_ptr[m_all];
+  info.dtype = s->dtype;
+  info.device = s->device;
+  int width = 1;
+  for (int i = 0; i < m_all; ++i) width = std::max(width, row_ptr[i + 1] - row_ptr[i]);
+  info.width = width;
+
+  // prepare_bounds (bounds.py:320-326): singleton inequality rows.
+  std::vector<char> is_bound(m_all, 0);
+  for (int i = 0; i < mi; ++i) {
+    const int r = me + i;
+    if (row_ptr[r + 1] - row_ptr[r] == 1) {
+      is_bound[r] = 1;
+      plan->bound_rows.push_back(r);
+      plan->bound_slots.push_back(row_ptr[r]);
+      plan->bound_vars.push_back(col[row_ptr[r]]);
+    }
+  }
+  // Kept rows (bounds.py:22-32), their CSR and the public-slot map.
+  std::vector<int32_t> krow_ptr(1, 0), kcol;
+  for (int r = 0; r < m_all; ++r) {
+    if (is_bound[r]) continue;
+    plan->kept_rows.push_back(r);
+    for (int k = row_ptr[r]; k < row_ptr[r + 1]; ++k) {
+      kcol.push_back(col[k]);
+      plan->kept_slots.push_back(k);
+    }
+    krow_ptr.push_back((int32_t)kcol.size());
+  }
+  plan->kept_row_ptr = krow_ptr;
+  plan->kept_cols = kcol;
+  info.kept_rows = (int)plan->kept_rows.size();
+  info.kept_nnz = (int)kcol.size();
+  info.bound_rows = (int)plan->bound_rows.size();
+
+  std::vector<int32_t> kcol_ptr, kcsc_row, kcsc_slot, acol_ptr, acsc_row, acsc_slot;
+  build_csc(n, krow_ptr, kcol, kcol_ptr, kcsc_row, kcsc_slot);
+  build_csc(n, row_ptr, col, acol_ptr, acsc_row, acsc_slot);
+  std::vector<int32_t> vb_ptr(n + 1, 0), vb_list(plan->bound_rows.size());
+  for (int32_t v : plan->bound_vars) vb_ptr[v + 1]++;
+  for (int j = 0; j < n; ++j) vb_ptr[j + 1] += vb_ptr[j];
+  {
+    std::vector<int32_t> fill(vb_ptr.begin(), vb_ptr.end() - 1);
+    for (size_t k = 0; k < plan->bound_vars.size(); ++k) vb_list[fill[plan->bound_vars[k]]++] = (int32_t)k;
+  }
+
+  // Pack every index array into one device block.
+  std::vector<const std::vector<int32_t>*> arrays = {
+      &krow_ptr, &kcol, &kcol_ptr, &kcsc_row, &kcsc_slot, &row_ptr, &col, &acol_ptr, &acsc_row,
+      &acsc_slot, &plan->kept_rows, &plan->kept_slots, &plan->bound_rows, &plan->bound_slots,
+      &plan->bound_vars, &vb_ptr, &vb_list};
+  std::vector<size_t> offsets;
+  size_t total = 0;
+  for (auto* a : arrays) {
+    offsets.push_back(total);
+    total += std::max<size_t>(a->size(), 1);
+    total = (total + 63) & ~(size_t)63;
+  }
+  std::vector<int32_t> host(total, 0);
+  for (size_t q = 0; q < arrays.size(); ++q)
+    if (!arrays[q]->empty()) std::memcpy(host.data() + offsets[q], arrays[q]->data(), arrays[q]->size() * 4);
+  {
+    DeviceGuard guard(s->device);
+    if (!guard.ok) {
+      delete plan;
+      return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+    }
+    cudaError_t e = cudaMalloc(&plan->device_block, total * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemcpy(plan->device_block, host.data(), total * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&plan->sm_count, cudaDevAttrMultiProcessorCount, s->device);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&plan->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, s->device);
+    if (e != cudaSuccess) {
+      if (plan->device_block) cudaFree(plan->device_block);
+      delete plan;
+      return cuda_fail(e, "purin_cp_plan_create");
+    }
+  }
+  const int32_t* d = static_cast<const int32_t*>(plan->device_block);
+  purin::DevStructure& st = plan->dev;
+  st.n = n;
+  st.me = me;
+  st.m = info.kept_rows;
+  st.nnz = info.kept_nnz;
+  st.row_ptr = d + offsets[0];
+  st.col = d + offsets[1];
+  st.col_ptr = d + offsets[2];
+  st.csc_row = d + offsets[3];
+  st.csc_slot = d + offsets[4];
+  st.m_all = m_all;
+  st.nnz_all = info.nnz;
+  st.row_ptr_all = d + offsets[5];
+  st.col_all = d + offsets[6];
+  st.col_ptr_all = d + offsets[7];
+  st.csc_row_all = d + offsets[8];
+  st.csc_slot_all = d + offsets[9];
+  st.kept_rows = d + offsets[10];
+  st.kept_slots = d + offsets[11];
+  st.n_bound = info.bound_rows;
+  st.bound_rows = d + offsets[12];
+  st.bound_slot = d + offsets[13];
+  st.bound_var = d + offsets[14];
+  st.var_bound_ptr = d + offsets[15];
+  st.var_bound_list = d + offsets[16];
+  *out = plan;
+  return PURIN_OK;
+}
+
+int32_t purin_cp_plan_destroy(PurinCpPlan* plan) {
+  if (!plan) return PURIN_OK;
+  if (plan->device_block) {
+    DeviceGuard guard(plan->info.device);
+    cudaFree(plan->device_block);
+  }
+  delete plan;
+  return PURIN_OK;
+}
+
+int32_t purin_cp_plan_info(const PurinCpPlan* plan, PurinCpPlanInfo* info) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (!info) return fail(PURIN_ERR_INVALID_ARGUMENT, "info is NULL");
+  *info = plan->info;
+  return PURIN_OK;
+}
+
+int32_t purin_cp_plan_indices(const PurinCpPlan* plan, int32_t which, int32_t* out) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (!out) return fail(PURIN_ERR_INVALID_ARGUMENT, "out is NULL");
+  const std::vector<int32_t>* v = nullptr;
+  switch (which) {
+    case PURIN_CP_KEPT_ROWS: v = &plan->kept_rows; break;
+    case PURIN_CP_KEPT_SLOTS: v = &plan->kept_slots; break;
+    case PURIN_CP_BOUND_ROWS: v = &plan->bound_rows; break;
+    case PURIN_CP_BOUND_SLOTS: v = &plan->bound_slots; break;
+    case PURIN_CP_BOUND_VARIABLES: v = &plan->bound_vars; break;
+    case PURIN_CP_KEPT_ROW_PTR: v = &plan->kept_row_ptr; break;
+    case PURIN_CP_KEPT_COLS: v = &plan->kept_cols; break;
+    default: return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown index array");
+  }
+  if (!v->empty()) std::memcpy(out, v->data(), v->size() * sizeof(int32_t));
+  return PURIN_OK;
+}
+
+int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t batch,
+                                const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
+                                size_t* bytes) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (!bytes) return fail(PURIN_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (int32_t r = check_config(config)) return r;
+  if (batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  *bytes = 0;
+  if (batch == 0) return PURIN_OK;
+  DeviceGuard guard(plan->info.device);
+  if (op == PURIN_CP_OP_FORWARD) {
+    *bytes = plan_forward(plan, config, batch).workspace;
+    return PURIN_OK;
+  }
+  if (op == PURIN_CP_OP_ADJOINT) {
+    if (int32_t r = check_linear(linear)) return r;
+    const AdjLayout L = plan_adjoint(plan, config, linear, batch);
+    if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
+    *bytes = L.total;
+    return PURIN_OK;
+  }
+  return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown op");
+}
+
+int32_t purin_cp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinCpForwardArgs* args,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  const int m = plan->info.kept_rows;
+  if (!args->target || !args->tolerance || !args->lower || !args->upper || !args->y || !args->iterations ||
+      !args->residual || !args->gap || !args->converged || (m > 0 && (!args->rhs || !args->dual)) ||
+      (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required forward array is NULL");
+  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or kept_nnz");
+  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64 ? run_forward<double>(plan, config, args, workspace, workspace_bytes, s)
+                                           : run_forward<float>(plan, config, args, workspace, workspace_bytes, s);
+}
+
+int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
+                         const PurinCpAdjointArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  const int m = plan->info.kept_rows;
+  if (!args->target || !args->lower || !args->upper || !args->y || !args->converged || !args->cot_y ||
+      (m > 0 && (!args->rhs || !args->dual)) || (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required adjoint array is NULL");
+  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or kept_nnz");
+  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64
+             ? run_adjoint<double>(plan, config, linear, args, workspace, workspace_bytes, s)
+             : run_adjoint<float>(plan, config, linear, args, workspace, workspace_bytes, s);
+}
+
+int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  const int me = plan->info.equality_size, mi = plan->info.inequality_size, m = plan->info.kept_rows;
+  if (!args->target || !args->lower || !args->upper || !args->y || !args->gap || !args->cp_converged ||
+      !args->status || !args->residual_inf_norm || !args->finite || !args->gradient_eligible ||
+      (me > 0 && !args->multipliers_eq) || (mi > 0 && (!args->multipliers_ineq || !args->slacks)) ||
+      (m > 0 && (!args->dual || !args->scale)) || (me + mi > 0 && !args->rhs_all) ||
+      (plan->info.nnz > 0 && !args->values_all))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required postprocess array is NULL");
+  if (args->values_all_stride != 0 && args->values_all_stride != plan->info.nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_all_stride must be 0 or nnz");
+  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64 ? run_post<double>(plan, args, s) : run_post<float>(plan, args, s);
+}
+
+}  // extern "C"

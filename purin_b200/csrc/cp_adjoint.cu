@@ -1,0 +1,635 @@
+// Implicit-differentiation VJP of the CP projection: the custom-VJP backward of
+// src/purin/solvers/chambolle_pock/bounds.py:80-165 (solver.py:186-272 without
+// bounds).
+//
+//   1. step sizes tau = s/(1+L), sigma = s/L with L from the seeded power
+//      iteration (bounds.py:87-101, kernels.py:52-65), or the diagonal steps
+//      (kernels.py:76-88) for fixed-step diagonal preconditioning;
+//   2. the linearisation of one fixed-step CP update at the forward solution
+//      (bounds.py:109-129), stored as lambda+ and per-element derivative codes
+//      of the clip / max operations (JAX's tie rule: half to each argument);
+//   3. restarted GMRES (primal_dual_interior_point/operators.py:792-1125) on
+//      (I - J^T) v = g with g = (cot_y masked by convergence, 0, 0);
+//   4. validity masking and the parameter pullback (bounds.py:148-165).
+//
+// The whole computation is ONE cooperative persistent kernel.  Samples are
+// assigned to CTAs statically (X = blockIdx.x + k * gridDim.x); a CTA keeps the
+// current Krylov vector and the pullback temporaries of its sample in shared
+// memory and its Krylov basis in a per-CTA global slot, so the basis workspace
+// scales with the number of resident CTAs, not with the batch.  GMRES cycles
+// run in lockstep across the batch, exactly like the reference's batched
+// while-loops: a bounded grid barrier after every cycle publishes the cycle
+// length (the largest number of Arnoldi steps any sample took) and the count
+// of samples still above their threshold, which set the shared iteration
+// budget and the loop condition (operators.py:919-1103).
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "cp_kernels.cuh"
+
+namespace purin {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 8;  // basis vectors per register-resident dot-product chunk
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += shfl_xor(v, o);
+  return v;
+}
+template <typename T>
+__device__ __forceinline__ T warp_max(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = pmax(v, shfl_xor(v, o));
+  return v;
+}
+
+// Block-wide reductions; every thread receives the result.
+template <typename T>
+__device__ T block_sum(T v, T* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  T total = T(0);
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) total = total + red[w];
+  __syncthreads();
+  return total;
+}
+template <typename T>
+__device__ T block_max(T v, T* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  T total = T(0);
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) total = pmax(total, red[w]);
+  __syncthreads();
+  return total;
+}
+__device__ __forceinline__ int block_and(int v) {
+  return __syncthreads_and(v);
+}
+
+template <typename T>
+struct Sample {
+  const T* vals;
+  const T* tgt;
+  const T* rhs;
+  const T* lo;
+  const T* up;
+  const T* ys;     // forward solution y* (also ybar at the linearisation point)
+  const T* ds;     // forward duals
+  const T* cot;    // cotangent of y
+  bool conv;
+  T* lamp;         // lambda+ at the linearisation point
+  uint8_t* yc;     // per-column derivative codes
+  uint8_t* dc;     // per-row derivative codes
+  T a, d, sigma;   // scalar steps
+  const T* av;     // diagonal steps (or null)
+  const T* dv;
+  const T* sv;
+};
+
+template <typename T>
+__device__ Sample<T> make_sample(const AdjParams<T>& p, int64_t X) {
+  const int n = p.st.n, m = p.st.m;
+  Sample<T> s;
+  s.vals = p.values + X * p.values_stride;
+  s.tgt = p.target + X * n;
+  s.rhs = p.rhs + X * m;
+  s.lo = p.lower + X * p.bounds_stride;
+  s.up = p.upper + X * p.bounds_stride;
+  s.ys = p.y + X * n;
+  s.ds = p.dual + X * m;
+  s.cot = p.cot_y + X * n;
+  s.conv = p.converged[X] != 0;
+  s.lamp = p.lamp + X * m;
+  s.yc = p.ycode + X * n;
+  s.dc = p.dcode + X * m;
+  if (p.diag) {
+    T* base = p.dsteps + X * (2 * (int64_t)n + m);
+    s.av = base;
+    s.dv = base + n;
+    s.sv = base + 2 * n;
+    s.a = s.d = s.sigma = T(0);
+  } else {
+    const T tau = p.steps[2 * X], sigma = p.steps[2 * X + 1];
+    s.a = T(1) / (T(1) + tau * T(1));
+    s.d = tau * s.a;
+    s.sigma = sigma;
+    s.av = s.dv = s.sv = nullptr;
+  }
+  return s;
+}
+
+// z <- z - J^T z for the packed state z = (y, dual, ybar) (bounds.py:130).
+template <typename T>
+__device__ void apply_operator(const DevStructure& st, const Sample<T>& s, T* buf, T* tn, T* tm) {
+  const int n = st.n, m = st.m, me = st.me;
+  T* zy = buf;
+  T* zd = buf + n;
+  T* zb = buf + n + m;
+  for (int j = threadIdx.x; j < n; j += kThreads) {
+    const T vy = zy[j], vb = zb[j];
+    const T gg = (vy + vb) + vb;
+    const T graw = gg * code_factor<T>(s.yc[j] & 3);
+    const T aa = s.av ? s.av[j] : s.a;
+    const T dd = s.dv ? s.dv[j] : s.d;
+    tn[j] = dd * (-graw);
+    zy[j] = vy - (aa * graw - vb);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += kThreads) {
+    T acc = T(0);
+    for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * tn[st.col[k]];
+    const T mu = zd[i] + acc;
+    const T mur = i < me ? mu : mu * balanced_factor<T>(s.dc[i]);
+    const T sg = s.sv ? s.sv[i] : s.sigma;
+    tm[i] = sg * mur;
+    zd[i] = zd[i] - mur;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += kThreads) {
+    T acc = T(0);
+    for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+      acc = acc + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
+    zb[j] = zb[j] - acc;
+  }
+  __syncthreads();
+}
+
+// g = (where(converged, cot_y, 0), 0, 0) entry e.
+template <typename T>
+__device__ __forceinline__ T rhs_entry(const Sample<T>& s, int n, int e) {
+  return (e < n && s.conv) ? s.cot[e] : T(0);
+}
+
+// Dot products of buf with basis rows [0, r) into out[0, r) (CGS pass, first half).
+template <typename T>
+__device__ void basis_dots(const T* V, int W, const T* buf, int r, T* out, T* red) {
+  for (int c0 = 0; c0 < r; c0 += kChunk) {
+    T part[kChunk];
+#pragma unroll
+    for (int q = 0; q < kChunk; ++q) part[q] = T(0);
+    for (int e = threadIdx.x; e < W; e += kThreads) {
+      const T be = buf[e];
+#pragma unroll
+      for (int q = 0; q < kChunk; ++q)
+        if (c0 + q < r) part[q] = part[q] + V[(size_t)(c0 + q) * W + e] * be;
+    }
+#pragma unroll
+    for (int q = 0; q < kChunk; ++q) part[q] = warp_sum(part[q]);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+      for (int q = 0; q < kChunk; ++q) red[(threadIdx.x >> 5) * kChunk + q] = part[q];
+    }
+    __syncthreads();
+    if (threadIdx.x < kChunk && c0 + (int)threadIdx.x < r) {
+      T total = T(0);
+      for (int w = 0; w < kWarps; ++w) total = total + red[w * kChunk + threadIdx.x];
+      out[c0 + threadIdx.x] = total;
+    }
+    __syncthreads();
+  }
+}
+
+// buf <- buf - sum_i c[i] V[i] over rows [0, r) (CGS pass, second half).
+template <typename T>
+__device__ void basis_update(const T* V, int W, T* buf, int r, const T* c) {
+  for (int e = threadIdx.x; e < W; e += kThreads) {
+    T acc = T(0);
+    for (int i = 0; i < r; ++i) acc = acc + c[i] * V[(size_t)i * W + e];
+    buf[e] = buf[e] - acc;
+  }
+  __syncthreads();
+}
+
+// jnp.hypot: max * sqrt(1 + (min/max)^2).
+template <typename T>
+__device__ __forceinline__ T jax_hypot(T x, T y) {
+  const T a = fabs(x), b = fabs(y);
+  const bool inf = isinf(a) || isinf(b);
+  const T hi = pmax(a, b), lo = pmin(a, b);
+  const T safe = hi == T(0) ? T(1) : hi;
+  const T q = lo / safe;
+  const T r = hi == T(0) ? hi : hi * sqrt(T(1) + q * q);
+  return inf ? T(INFINITY) : r;
+}
+
+template <typename T, bool kSmem>
+__global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T> p) {
+  extern __shared__ __align__(16) unsigned char dyn[];
+  __shared__ int s_flag;
+  const DevStructure& st = p.st;
+  const int n = st.n, m = st.m, me = st.me;
+  const int W = 2 * n + m;
+  const int R = p.R;
+  T* sm = reinterpret_cast<T*>(dyn);
+  T *buf, *tn, *tm, *small;
+  if (kSmem) {
+    buf = sm;
+    tn = buf + W;
+    tm = tn + n;
+    small = tm + m;
+  } else {
+    buf = p.gbuf + (size_t)blockIdx.x * (W + n + m);
+    tn = buf + W;
+    tm = tn + n;
+    small = sm;
+  }
+  T* hess = small;              // (R + 1) x R, row-major
+  T* proj = hess + (R + 1) * R; // R + 1
+  T* cs = proj + (R + 1);       // R
+  T* sn = cs + R;               // R
+  T* coef = sn + R;             // R + 1
+  T* c2 = coef + (R + 1);       // R + 1
+  T* bsv = c2 + (R + 1);        // R
+  T* red = bsv + R;             // kWarps * kChunk
+  T* V = p.basis + (size_t)blockIdx.x * (R + 1) * W;
+  const T zero = T(0), one = T(1);
+  const T eps = T(1e-30), breakdown = T(1e-14);
+  const unsigned nblocks = gridDim.x;
+
+  // ---- phase 0: step sizes, linearisation, right-hand side ----------------
+  for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+    const T* vals = p.values + X * p.values_stride;
+    if (p.diag) {
+      T* base = p.dsteps + X * (2 * (int64_t)n + m);
+      for (int i = threadIdx.x; i < m; i += kThreads) {
+        T acc = zero;
+        for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + fabs(vals[k]) * one;
+        base[2 * n + i] = p.safety / (acc > zero ? pmax(acc, T(1e-12)) : one);
+      }
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        T acc = zero;
+        for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+          acc = acc + fabs(vals[st.csc_slot[e]]) * one;
+        const T tau = p.safety / (acc > zero ? pmax(acc, T(1e-12)) : one);
+        const T a = one / (one + tau * one);
+        base[j] = a;
+        base[n + j] = tau * a;
+      }
+    } else {
+      uint32_t k0, k1;
+      split_key(p.norm_seed, p.sample_offset + X, p.total_batch, p.partitionable != 0, k0, k1);
+      T* x = buf;
+      T ss = zero;
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        const T v = NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0);
+        x[j] = v;
+        ss = ss + v * v;
+      }
+      const T nrm = sqrt(block_sum(ss, red)) + T(1e-12);
+      for (int j = threadIdx.x; j < n; j += kThreads) x[j] = x[j] / nrm;
+      T eig = zero;
+      for (int it = 0; it < p.norm_iterations; ++it) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < m; i += kThreads) {
+          T acc = zero;
+          for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + vals[k] * x[st.col[k]];
+          tm[i] = acc;
+        }
+        __syncthreads();
+        T xz = zero, zz = zero;
+        for (int j = threadIdx.x; j < n; j += kThreads) {
+          T acc = zero;
+          for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+            acc = acc + vals[st.csc_slot[e]] * tm[st.csc_row[e]];
+          tn[j] = acc;
+          xz = xz + x[j] * acc;
+          zz = zz + acc * acc;
+        }
+        eig = block_sum(xz, red);
+        const T zn = sqrt(block_sum(zz, red)) + T(1e-12);
+        for (int j = threadIdx.x; j < n; j += kThreads) x[j] = tn[j] / zn;
+      }
+      const T L = pmax(sqrt(pmax(eig, zero)) + T(1e-12), T(1e-12));
+      if (threadIdx.x == 0) {
+        p.steps[2 * X] = p.safety / (one + L);
+        p.steps[2 * X + 1] = p.safety / L;
+      }
+    }
+    __syncthreads();
+    const Sample<T> s = make_sample(p, X);
+    // Linearisation point (y*, lambda*, ybar = y*): lambda+ and derivative codes.
+    for (int i = threadIdx.x; i < m; i += kThreads) {
+      T acc = zero;
+      for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * s.ys[st.col[k]];
+      const T sg = s.sv ? s.sv[i] : s.sigma;
+      const T raw = s.ds[i] + sg * (acc - s.rhs[i]);
+      const T lp = i < me ? raw : pmax(raw, zero);
+      s.dc[i] = (uint8_t)(i < me ? 2 : balanced_code(raw, lp, zero));
+      tm[i] = lp;
+      s.lamp[i] = lp;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += kThreads) {
+      T t = zero;
+      for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+        t = t + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
+      const T yo = s.ys[j];
+      const T c = -s.tgt[j];
+      const T aa = s.av ? s.av[j] : s.a;
+      const T dd = s.dv ? s.dv[j] : s.d;
+      const T yr = (aa * yo - dd * t) + (-dd) * c;
+      const T l = s.lo[j], u = s.up[j];
+      const T u1 = pmax(l, yr);
+      const T yn = pmin(u, u1);
+      const int d_u1 = balanced_code(u1, yn, u);
+      const int d_up = balanced_code(u, yn, u1);
+      const int d_raw = balanced_code(yr, u1, l);
+      const int d_lo = balanced_code(l, u1, yr);
+      s.yc[j] = (uint8_t)(product_code(d_u1, d_raw) | (product_code(d_u1, d_lo) << 2) | (d_up << 4));
+    }
+    __syncthreads();
+    // Right-hand side scale, threshold, x = 0 and the initial residual.
+    T gmax = zero;
+    for (int e = threadIdx.x; e < W; e += kThreads) {
+      gmax = pmax(gmax, fabs(rhs_entry(s, n, e)));
+      buf[e] = zero;
+      p.x[X * W + e] = zero;
+    }
+    gmax = block_max(gmax, red);
+    apply_operator(st, s, buf, tn, tm);
+    T r0 = zero;
+    for (int e = threadIdx.x; e < W; e += kThreads) r0 = pmax(r0, fabs(rhs_entry(s, n, e) - buf[e]));
+    r0 = block_max(r0, red);
+    if (threadIdx.x == 0) {
+      const T thr = pmax(p.lin_atol, p.lin_tol * gmax);
+      p.thresh[X] = thr;
+      p.resinf[X] = r0;
+      if (r0 > thr) atomicAdd(&p.cycle_act[0], 1u);
+    }
+    __syncthreads();
+  }
+
+  if (!grid_barrier(p.barrier, nblocks, p.timeout_ns)) {
+    if (threadIdx.x == 0) atomicExch(p.device_error, 1);
+    return;
+  }
+
+  // ---- GMRES cycles in lockstep over the batch ------------------------------
+  int completed = 0;
+  int cycle = 0;
+  bool any = atomicOr(&p.cycle_act[0], 0u) > 0;
+  while (completed < p.max_it && any) {
+    const int limit = min(R, p.max_it - completed);
+    for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+      const T thr = p.thresh[X];
+      if (!(p.resinf[X] > thr)) continue;  // not cycle-active: frozen
+      const Sample<T> s = make_sample(p, X);
+      T* x = p.x + X * W;
+      // residual = g - A x, normalised into V[0]
+      for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = x[e];
+      __syncthreads();
+      apply_operator(st, s, buf, tn, tm);
+      T ss = zero;
+      for (int e = threadIdx.x; e < W; e += kThreads) {
+        const T r = rhs_entry(s, n, e) - buf[e];
+        buf[e] = r;
+        ss = ss + r * r;
+      }
+      const T beta = sqrt(block_sum(ss, red));
+      const T safe_beta = pmax(beta, eps);
+      for (int e = threadIdx.x; e < W; e += kThreads) {
+        const T v = buf[e] / safe_beta;
+        buf[e] = v;
+        V[e] = v;
+      }
+      for (int q = threadIdx.x; q < (R + 1) * R; q += kThreads) hess[q] = zero;
+      for (int q = threadIdx.x; q < R + 1; q += kThreads) proj[q] = q == 0 ? beta : zero;
+      for (int q = threadIdx.x; q < R; q += kThreads) { cs[q] = zero; sn[q] = zero; }
+      if (threadIdx.x == 0) s_flag = 1;
+      __syncthreads();
+      int it = 0;
+      while (it < limit && s_flag) {
+        apply_operator(st, s, buf, tn, tm);
+        basis_dots(V, W, buf, it + 1, coef, red);
+        basis_update(V, W, buf, it + 1, coef);
+        basis_dots(V, W, buf, it + 1, c2, red);
+        basis_update(V, W, buf, it + 1, c2);
+        if (threadIdx.x <= it) coef[threadIdx.x] = coef[threadIdx.x] + c2[threadIdx.x];
+        T nsq = zero;
+        for (int e = threadIdx.x; e < W; e += kThreads) nsq = nsq + buf[e] * buf[e];
+        const T nn = sqrt(block_sum(nsq, red));
+        const T sn_ = pmax(nn, eps);
+        int fin = 1;
+        T* Vn = V + (size_t)(it + 1) * W;
+        for (int e = threadIdx.x; e < W; e += kThreads) {
+          const T v = buf[e] / sn_;
+          buf[e] = v;
+          Vn[e] = v;
+          fin &= finite(v) ? 1 : 0;
+        }
+        fin = block_and(fin);
+        if (threadIdx.x == 0) {
+          // column of the Hessenberg matrix with previous rotations applied
+          T* col = c2;  // reuse as scratch column of length R + 1
+          for (int q = 0; q <= R; ++q) col[q] = q < R && q <= it ? coef[q] : zero;
+          col[it + 1] = nn;
+          for (int r = 0; r < it; ++r) {
+            const T f = col[r], g2 = col[r + 1];
+            col[r] = cs[r] * f + sn[r] * g2;
+            col[r + 1] = -sn[r] * f + cs[r] * g2;
+          }
+          const T diag = col[it], sub = col[it + 1];
+          const T rot = jax_hypot(diag, sub);
+          const T safe_rot = pmax(rot, eps);
+          const bool big = rot > eps;
+          const T nc = big ? diag / safe_rot : one;
+          const T ns = big ? sub / safe_rot : zero;
+          cs[it] = nc;
+          sn[it] = ns;
+          col[it] = rot;
+          col[it + 1] = zero;
+          for (int q = 0; q <= R; ++q) hess[q * R + it] = col[q];
+          const T cur = proj[it], nxt = proj[it + 1];
+          const T rc = nc * cur + ns * nxt;
+          const T rn = -ns * cur + nc * nxt;
+          proj[it] = rc;
+          proj[it + 1] = rn;
+          const T estimate = fabs(rn);
+          const bool ok = finite(estimate) && finite(rot) && fin;
+          const bool happy = nn <= breakdown;
+          s_flag = (ok && !happy && estimate > thr) ? 1 : 0;
+        }
+        __syncthreads();
+        ++it;
+      }
+      const int row_steps = it;
+      if (threadIdx.x == 0) {
+        for (int q = 0; q < R; ++q) bsv[q] = zero;
+        for (int rev = 0; rev < R; ++rev) {
+          const int row = R - 1 - rev;
+          T trailing = zero;
+          for (int q = 0; q < R; ++q) trailing = trailing + hess[row * R + q] * bsv[q];
+          const T numerator = proj[row] - trailing;
+          const T diag = hess[row * R + row];
+          const T safe = fabs(diag) > eps ? diag : one;
+          const T value = numerator / safe;
+          bsv[row] = row < row_steps ? value : zero;
+        }
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < W; e += kThreads) {
+        T corr = zero;
+        for (int q = 0; q < R; ++q) {
+          if (q < row_steps) corr = corr + bsv[q] * V[(size_t)q * W + e];
+        }
+        const T cand = x[e] + corr;
+        buf[e] = cand;
+        x[e] = cand;
+      }
+      __syncthreads();
+      apply_operator(st, s, buf, tn, tm);
+      T cn = zero;
+      for (int e = threadIdx.x; e < W; e += kThreads) cn = pmax(cn, fabs(rhs_entry(s, n, e) - buf[e]));
+      cn = block_max(cn, red);
+      if (threadIdx.x == 0) {
+        p.resinf[X] = cn;
+        atomicMax(&p.cycle_len[cycle], (unsigned)row_steps);
+        if (cn > thr) atomicAdd(&p.cycle_act[cycle + 1], 1u);
+      }
+      __syncthreads();
+    }
+    if (!grid_barrier(p.barrier, nblocks, p.timeout_ns)) {
+      if (threadIdx.x == 0) atomicExch(p.device_error, 1);
+      return;
+    }
+    completed += (int)atomicOr(&p.cycle_len[cycle], 0u);
+    any = atomicOr(&p.cycle_act[cycle + 1], 0u) > 0;
+    ++cycle;
+  }
+
+  // ---- validity and parameter pullback (bounds.py:148-165) ------------------
+  for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+    const Sample<T> s = make_sample(p, X);
+    const T* x = p.x + X * W;
+    int fin = 1;
+    for (int e = threadIdx.x; e < W; e += kThreads) {
+      const T v = x[e];
+      buf[e] = v;
+      fin &= finite(v) ? 1 : 0;
+    }
+    fin = block_and(fin);
+    const T ri = p.resinf[X];
+    const T thr = p.thresh[X];
+    const bool fin_all = fin && finite(ri);
+    const int code = !fin_all ? 2 : (ri <= thr ? 0 : 1);
+    const bool valid = s.conv && fin && finite(ri) && (code == 0 || ri <= p.adj_tol);
+    if (!valid) {
+      for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = zero;
+    }
+    __syncthreads();
+    const T* zy = buf;
+    const T* zd = buf + n;
+    const T* zb = buf + n + m;
+    for (int j = threadIdx.x; j < n; j += kThreads) {
+      const T vy = zy[j], vb = zb[j];
+      const T gg = (vy + vb) + vb;
+      const int code_j = s.yc[j];
+      const T graw = gg * code_factor<T>(code_j & 3);
+      const T glo = gg * code_factor<T>((code_j >> 2) & 3);
+      const T gup = gg * balanced_factor<T>((code_j >> 4) & 3);
+      const T dd = s.dv ? s.dv[j] : s.d;
+      tn[j] = dd * (-graw);
+      if (p.g_target) p.g_target[X * n + j] = clean(dd * graw);
+      if (p.g_lower) p.g_lower[X * n + j] = clean(glo);
+      if (p.g_upper) p.g_upper[X * n + j] = clean(gup);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < m; i += kThreads) {
+      T acc = zero;
+      for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * tn[st.col[k]];
+      const T mu = zd[i] + acc;
+      const T mur = i < me ? mu : mu * balanced_factor<T>(s.dc[i]);
+      const T sg = s.sv ? s.sv[i] : s.sigma;
+      const T w = sg * mur;
+      if (p.g_rhs) p.g_rhs[X * m + i] = clean(-w);
+      if (p.g_values) {
+        const T lp = s.lamp[i];
+        T* gv = p.g_values + X * st.nnz;
+        for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) {
+          const int j = st.col[k];
+          gv[k] = clean(w * s.ys[j] + tn[j] * lp);
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      if (p.lin_status) p.lin_status[X] = code;
+      if (p.lin_residual) p.lin_residual[X] = ri;
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+size_t small_elems(int R) {
+  return (size_t)(R + 1) * R + (R + 1) + 2 * (size_t)R + 2 * (size_t)(R + 1) + R + kWarps * kChunk;
+}
+
+}  // namespace
+
+template <typename T>
+size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors) {
+  const size_t W = 2 * (size_t)n + m;
+  size_t elems = small_elems<T>(R);
+  if (smem_vectors) elems += W + n + m;
+  return elems * sizeof(T);
+}
+
+template <typename T>
+int adjoint_grid(int sm_count, int n, int m, int R, bool smem_vectors, int64_t batch) {
+  const size_t smem = adjoint_smem_bytes<T>(n, m, R, smem_vectors);
+  int per_sm = 0;
+  if (smem_vectors) {
+    auto kern = cp_adjoint_kernel<T, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+      return 0;
+  } else {
+    auto kern = cp_adjoint_kernel<T, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+      return 0;
+  }
+  int64_t grid = (int64_t)per_sm * sm_count;
+  if (grid > batch) grid = batch;
+  return (int)grid;
+}
+
+template <typename T>
+cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors, cudaStream_t stream) {
+  const int n = p.st.n, m = p.st.m;
+  const size_t smem = adjoint_smem_bytes<T>(n, m, p.R, smem_vectors);
+  void* args[] = {(void*)&p};
+  if (smem_vectors) {
+    auto kern = cp_adjoint_kernel<T, true>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
+  }
+  auto kern = cp_adjoint_kernel<T, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
+}
+
+template size_t adjoint_smem_bytes<double>(int, int, int, bool);
+template size_t adjoint_smem_bytes<float>(int, int, int, bool);
+template int adjoint_grid<double>(int, int, int, int, bool, int64_t);
+template int adjoint_grid<float>(int, int, int, int, bool, int64_t);
+template cudaError_t launch_adjoint<double>(const AdjParams<double>&, int, bool, cudaStream_t);
+template cudaError_t launch_adjoint<float>(const AdjParams<float>&, int, bool, cudaStream_t);
+
+}  // namespace purin

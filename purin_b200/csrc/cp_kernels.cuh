@@ -1,0 +1,143 @@
+// Kernel parameter blocks and launchers shared by the C ABI (capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "plan.cuh"
+
+namespace purin {
+
+template <typename T>
+struct FwdParams {
+  DevStructure st;
+  int64_t batch;
+  const T* values;
+  int64_t values_stride;
+  const T* rhs;
+  const T* target;
+  const T* dual0;
+  const T* tol;
+  const T* lower;
+  const T* upper;
+  int64_t bounds_stride;
+  const uint8_t* feasible;
+  int64_t sample_offset;
+  int64_t total_batch;
+  T* y_out;
+  T* dual_out;
+  int32_t* it_out;
+  T* res_out;
+  T* gap_out;
+  uint8_t* conv_out;
+  int max_iterations;
+  int accelerated;
+  T safety;
+  int norm_iterations;
+  int64_t norm_seed;
+  int norm_bound;
+  int diag;
+  int partitionable;
+  T* gstate;  // per-tile state in global memory when it does not fit in shared memory
+};
+
+template <typename T>
+struct AdjParams {
+  DevStructure st;
+  int64_t batch;
+  const T* values;
+  int64_t values_stride;
+  const T* rhs;
+  const T* target;
+  const T* lower;
+  const T* upper;
+  int64_t bounds_stride;
+  const T* y;
+  const T* dual;
+  const uint8_t* converged;
+  const T* cot_y;
+  int64_t sample_offset;
+  int64_t total_batch;
+  T* g_values;
+  T* g_rhs;
+  T* g_target;
+  T* g_lower;
+  T* g_upper;
+  int32_t* lin_status;
+  T* lin_residual;
+  int32_t* device_error;
+  // configuration
+  int accelerated;
+  int diag;
+  int norm_iterations;
+  int partitionable;
+  int64_t norm_seed;
+  T safety;
+  T lin_tol;
+  T lin_atol;
+  T adj_tol;
+  int R;       // effective restart = min(restart, max_iterations, W)
+  int max_it;  // GMRES iteration budget
+  uint64_t timeout_ns;
+  // workspace
+  T* x;            // B * W
+  T* lamp;         // B * m
+  uint8_t* ycode;  // B * n
+  uint8_t* dcode;  // B * m
+  T* steps;        // B * 2 : tau, sigma
+  T* dsteps;       // B * (2n + m) : a, d (per column), sigma (per row); diagonal steps only
+  T* thresh;       // B
+  T* resinf;       // B
+  T* basis;        // grid * (R + 1) * W
+  T* gbuf;         // grid * (W + n + m) when the vectors do not fit in shared memory
+  unsigned* cycle_len;  // max_it + 2
+  unsigned* cycle_act;  // max_it + 2
+  GridBarrier* barrier;
+};
+
+template <typename T>
+struct PostParams {
+  DevStructure st;
+  int64_t batch;
+  const T* values_all;
+  int64_t values_stride;
+  const T* rhs_all;
+  const T* target;
+  const T* lower;
+  const T* upper;
+  int64_t bounds_stride;
+  const T* scale;
+  const T* y;
+  const T* dual;
+  const T* gap;
+  const uint8_t* cp_conv;
+  T tol;
+  T* meq;
+  T* miq;
+  T* slacks;
+  int32_t* status;
+  T* resid;
+  uint8_t* finite;
+  uint8_t* elig;
+};
+
+template <typename T>
+cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
+                           cudaStream_t stream);
+template <typename T>
+size_t forward_static_smem(int S);
+
+// Adjoint: shared-memory bytes for one CTA, occupancy-limited cooperative grid.
+template <typename T>
+size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors);
+template <typename T>
+int adjoint_grid(int device_sm_count, int n, int m, int R, bool smem_vectors, int64_t batch);
+template <typename T>
+cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors,
+                           cudaStream_t stream);
+
+template <typename T>
+cudaError_t launch_post(const PostParams<T>& p, cudaStream_t stream);
+
+}  // namespace purin

@@ -1,0 +1,60 @@
+// Device-resident sparse structure of a prepared CP projection.
+//
+// Built once per plan (PreparedChambollePockProjection.__post_init__,
+// src/purin/solvers/chambolle_pock/solver.py:32-65).  The reference keeps a
+// padded ELL layout (kernels.py:26-40) and performs K.T products as scatters
+// (linalg/sparse/operators.py:521-533); here the same pattern is stored as CSR
+// for K @ x and as CSC (entries sorted by row, i.e. the scatter's update order)
+// for K.T @ y, so both products are gathers with deterministic summation order.
+#pragma once
+
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/purin_cp.h"
+
+namespace purin {
+
+struct DevStructure {
+  int n;
+  int me;
+  int m;       // kept rows: me + kept inequality rows
+  int nnz;     // kept nonzeros
+  // Kept rows (the CP operator K).
+  const int* row_ptr;   // m + 1
+  const int* col;       // nnz
+  const int* col_ptr;   // n + 1
+  const int* csc_row;   // nnz, kept row index, ascending per column
+  const int* csc_slot;  // nnz, kept CSR slot
+  // All public rows (post-processing).
+  int m_all;
+  int nnz_all;
+  const int* row_ptr_all;
+  const int* col_all;
+  const int* col_ptr_all;
+  const int* csc_row_all;
+  const int* csc_slot_all;
+  const int* kept_rows;   // m: public row index
+  const int* kept_slots;  // nnz: public CSR slot
+  // Bound rows (singleton inequalities turned into box bounds).
+  int n_bound;
+  const int* bound_rows;
+  const int* bound_slot;
+  const int* bound_var;
+  const int* var_bound_ptr;   // n + 1
+  const int* var_bound_list;  // n_bound, bound index k per variable
+};
+
+}  // namespace purin
+
+struct PurinCpPlan {
+  PurinCpPlanInfo info;
+  purin::DevStructure dev;
+  void* device_block = nullptr;  // one cudaMalloc holding every index array
+  // Host copies for purin_cp_plan_indices.
+  std::vector<int32_t> kept_rows, kept_slots, bound_rows, bound_slots, bound_vars;
+  std::vector<int32_t> kept_row_ptr, kept_cols;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+};

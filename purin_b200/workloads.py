@@ -1,0 +1,171 @@
+"""Seeded synthetic problems of the five benchmark configurations.
+
+No public dataset is involved: every configuration is generated from
+``numpy.random.default_rng(seed)`` (seed 0 by default) in a fixed order --
+structure, then bounds, then per-sample x0, then slack, then candidates, then
+loss targets -- as ParametricQP problems whose variable bounds are singleton
+inequality rows (x_i <= u_i, -x_i <= -l_i) that the CP layer's bound presolve
+turns into box bounds.  Per-sample right-hand sides enter through identity
+parameter maps, so parameters are ``theta = [b; h]``.
+
+    0  fp64, B=256,   n=64,    me=32,   mi=32,   4 nnz/row,  l=-1, u=1, fixed-step 500 it
+    1  fp64/fp32, B=4096, n=1024, me=256, mi=512, 8 nnz/row, l~U(-2,-.5), u~U(.5,2), accel 1000 it
+    2  fp64, B=2048,  n=2048,  me=512,  mi=1024, 8 nnz/row, loss 0.5||y-t||^2, 2000 it (+VJP)
+    3  fp32, B=16384, network flow: 5000 nodes, 20000 edges, 4000 coupling rows, 1500 it
+    4  fp32/fp64, B in {1,64,1024,16384,65536}, n=4096, me=1024, mi=2048, 16 nnz/row,
+       WeightedDistance w~U(.5,2), accel 1000 it
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import scipy.sparse as sp
+
+from purin_b200.config import ChambollePockConfig, ImplicitGradientConfig
+from purin_b200.problems import ParametricQP
+
+
+@dataclass
+class Workload:
+    name: str
+    problem: ParametricQP
+    theta: np.ndarray
+    candidates: np.ndarray
+    config: ChambollePockConfig
+    dtype: str
+    targets: np.ndarray | None = None
+    weights: np.ndarray | None = None
+    info: dict = field(default_factory=dict)
+
+
+def _random_rows(rng, rows, n, k):
+    indptr = np.arange(rows + 1, dtype=np.int64) * k
+    indices = np.concatenate([rng.choice(n, k, replace=False) for _ in range(rows)]) if rows else (
+        np.zeros(0, np.int64))
+    data = rng.normal(size=rows * k)
+    return sp.csr_matrix((data, indices, indptr), shape=(rows, n))
+
+
+def _box_qp(A_eq, A_in, lower, upper, name):
+    """ParametricQP with equality rows A_eq y = b, A_in y <= h and box bounds as singleton rows."""
+    me, n = A_eq.shape
+    mi = A_in.shape[0]
+    eye = sp.identity(n, format="csr")
+    A_ineq = sp.vstack([A_in, eye, -eye], format="csr")
+    p = me + mi
+    b_eq_map = sp.hstack([sp.identity(me), sp.csr_matrix((me, mi))], format="csr")
+    b_in_map = sp.vstack([sp.hstack([sp.csr_matrix((mi, me)), sp.identity(mi)]),
+                          sp.csr_matrix((2 * n, p))], format="csr")
+    b_ineq0 = np.concatenate([np.zeros(mi), upper, -lower])
+    return ParametricQP(P=sp.identity(n, format="csr"), q0=np.zeros(n), A_eq=A_eq,
+                        b_eq0=np.zeros(me), b_eq_parameter_map=b_eq_map, A_ineq=A_ineq,
+                        b_ineq0=b_ineq0, b_ineq_parameter_map=b_in_map, name=name)
+
+
+def random_box_config(*, batch, n, me, mi, nnz, bounds, seed=0, name="cp"):
+    """Configs 0-2 and 4: random rows, seeded feasible x0, candidates 2 N(0,1)."""
+    rng = np.random.default_rng(seed)
+    A_eq = _random_rows(rng, me, n, nnz)
+    A_in = _random_rows(rng, mi, n, nnz)
+    if bounds == "unit":
+        lower, upper = -np.ones(n), np.ones(n)
+    else:
+        lower = rng.uniform(-2.0, -0.5, n)
+        upper = rng.uniform(0.5, 2.0, n)
+    x0 = rng.uniform(-0.5, 0.5, (batch, n))
+    slack = rng.uniform(0.0, 0.1, (batch, mi))
+    candidates = 2.0 * rng.normal(size=(batch, n))
+    b = (A_eq @ x0.T).T
+    h = (A_in @ x0.T).T + slack
+    theta = np.concatenate([b, h], axis=1)
+    problem = _box_qp(A_eq, A_in, lower, upper, name)
+    return problem, theta, candidates, rng
+
+
+def network_flow_config(*, batch, nodes=5000, edges=20000, couplings=4000, seed=0):
+    """Config 3: node-incidence conservation, 2-edge coupling rows, |x| <= cap."""
+    rng = np.random.default_rng(seed)
+    order = rng.permutation(nodes)
+    pairs = set()
+    heads, tails = [], []
+    for k in range(1, nodes):
+        a, b = int(order[k]), int(order[rng.integers(0, k)])
+        pairs.add((min(a, b), max(a, b)))
+        heads.append(a)
+        tails.append(b)
+    while len(heads) < edges:
+        a, b = (int(v) for v in rng.integers(0, nodes, 2))
+        if a == b or (min(a, b), max(a, b)) in pairs:
+            continue
+        pairs.add((min(a, b), max(a, b)))
+        heads.append(a)
+        tails.append(b)
+    heads = np.asarray(heads)
+    tails = np.asarray(tails)
+    flip = rng.random(edges) < 0.5
+    heads, tails = np.where(flip, tails, heads), np.where(flip, heads, tails)
+    cols = np.arange(edges)
+    incidence = sp.csr_matrix(
+        (np.concatenate([np.ones(edges), -np.ones(edges)]),
+         (np.concatenate([heads, tails]), np.concatenate([cols, cols]))), shape=(nodes, edges))
+    incidence.sort_indices()
+    crow = np.repeat(np.arange(couplings), 2)
+    ccol = np.concatenate([rng.choice(edges, 2, replace=False) for _ in range(couplings)])
+    cval = rng.choice([-1.0, 1.0], size=2 * couplings)
+    coupling = sp.csr_matrix((cval, ccol, np.arange(couplings + 1) * 2), shape=(couplings, edges))
+    cap = rng.uniform(1.0, 3.0, edges)
+    demand = rng.normal(size=(batch, nodes))
+    demand -= demand.mean(axis=1, keepdims=True)
+    h = rng.uniform(0.5, 1.5, (batch, couplings))
+    candidates = 3.0 * rng.normal(size=(batch, edges))
+    theta = np.concatenate([demand, h], axis=1)
+    problem = _box_qp(incidence, coupling, -cap, cap, "network_flow")
+    return problem, theta, candidates
+
+
+def make_workload(index: int, batch: int | None = None, *, dtype: str | None = None,
+                  seed: int = 0, mode: str = "fixed") -> Workload:
+    """Workload of benchmark configuration ``index`` (0-4).
+
+    ``mode="fixed"`` keeps the reference's stopping test and per-sample freeze
+    with the configuration's iteration budget; ``mode="converged"`` (config 1)
+    uses tolerance 1e-6.
+    """
+    if index == 0:
+        batch = 256 if batch is None else batch
+        problem, theta, cand, _ = random_box_config(batch=batch, n=64, me=32, mi=32, nnz=4,
+                                                    bounds="unit", seed=seed, name="config0")
+        cfg = ChambollePockConfig(accelerated=False, max_iterations=500)
+        return Workload("config0", problem, theta, cand, cfg, dtype or "float64")
+    if index == 1:
+        batch = 4096 if batch is None else batch
+        problem, theta, cand, _ = random_box_config(batch=batch, n=1024, me=256, mi=512, nnz=8,
+                                                    bounds="random", seed=seed, name="config1")
+        cfg = ChambollePockConfig(accelerated=True, max_iterations=1000,
+                                  tolerance=1e-6 if mode == "converged" else 1e-9)
+        return Workload("config1", problem, theta, cand, cfg, dtype or "float64")
+    if index == 2:
+        batch = 2048 if batch is None else batch
+        problem, theta, cand, rng = random_box_config(batch=batch, n=2048, me=512, mi=1024, nnz=8,
+                                                      bounds="random", seed=seed, name="config2")
+        targets = rng.normal(size=(batch, 2048))
+        cfg = ChambollePockConfig(
+            max_iterations=2000,
+            implicit_gradient=ImplicitGradientConfig(differentiate_problem_parameters=True))
+        return Workload("config2", problem, theta, cand, cfg, dtype or "float64", targets=targets)
+    if index == 3:
+        batch = 16384 if batch is None else batch
+        problem, theta, cand = network_flow_config(batch=batch, seed=seed)
+        cfg = ChambollePockConfig(max_iterations=1500)
+        return Workload("config3", problem, theta, cand, cfg, dtype or "float32")
+    if index == 4:
+        batch = 1024 if batch is None else batch
+        problem, theta, cand, rng = random_box_config(batch=batch, n=4096, me=1024, mi=2048,
+                                                      nnz=16, bounds="random", seed=seed,
+                                                      name="config4")
+        weights = rng.uniform(0.5, 2.0, 4096)
+        cfg = ChambollePockConfig(accelerated=True, max_iterations=1000)
+        return Workload("config4", problem, theta, cand, cfg, dtype or "float32", weights=weights)
+    raise ValueError("configuration index must be 0..4")

@@ -1,0 +1,139 @@
+"""Shared test helpers: reference-test problems and the canonical -> oracle bridge."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from oracle.projection import OracleConfig, OracleProjection
+from oracle.sparse import layout
+from purin_b200.problems import Projection, canonical_of
+
+
+def make_problem(*, inequalities=False, nonlinear=False):
+    """``tests/test_projections.py:33-45`` of the reference."""
+    problem = Projection()
+    p = problem.add_parameter(["b"])
+    y = problem.add_variable(["u", "v"])
+    problem.objective = 0.0
+    if nonlinear:
+        problem.constraints.add(y.u**2 + y.v**2 <= p.b)
+    else:
+        problem.constraints.add(y.u + y.v == p.b)
+        if inequalities:
+            problem.constraints.add(y.u >= 0)
+            problem.constraints.add(y.v >= 0)
+    return problem
+
+
+def regression_problem():
+    """``tests/test_regression_chambolle_pock.py:16-22`` of the reference."""
+    p = Projection(method="chambolle-pock")
+    t = p.add_parameter(["b"])
+    y = p.add_variable(["u", "v"])
+    p.objective = 0.0
+    p.constraints.add(y.u + y.v == t.b, y.u >= 0)
+    return p
+
+
+def oracle_config(cfg) -> OracleConfig:
+    """OracleConfig from a purin_b200 ChambollePockConfig."""
+    return OracleConfig(
+        tolerance=cfg.tolerance, max_iterations=cfg.max_iterations, accelerated=cfg.accelerated,
+        safety=cfg.safety, norm_iterations=cfg.norm_iterations, norm_seed=cfg.norm_seed,
+        row_scaling=cfg.row_scaling, norm_bound=cfg.norm_bound,
+        diagonal_preconditioning=cfg.diagonal_preconditioning,
+        linear_tolerance=cfg.linear_solver.tolerance, linear_atol=cfg.linear_solver.atol,
+        linear_restart=cfg.linear_solver.restart,
+        linear_max_iterations=cfg.linear_solver.max_iterations,
+        adjoint_tolerance=cfg.implicit_gradient.adjoint_tolerance)
+
+
+def to_ell(canonical, values_csr):
+    """CSR-slot values (1|B, nnz) -> padded ELL (B, m_all, width) of the reference layout."""
+    rows = list(canonical.equality_sparsity) + list(canonical.inequality_sparsity)
+    support, mask, positions = layout(rows, canonical.variable_size)
+    batch = values_csr.shape[0]
+    out = np.zeros((batch, support.shape[0] * support.shape[1]), dtype=values_csr.dtype)
+    out[:, positions] = values_csr
+    return out.reshape(batch, support.shape[0], support.shape[1])
+
+
+class OracleLayer:
+    """A problem + config evaluated by the oracle (values from the product frontend)."""
+
+    def __init__(self, problem, cfg, dtype=np.float64, partitionable=True):
+        self.canonical = canonical_of(problem)
+        self.cfg = cfg
+        self.dtype = np.dtype(dtype)
+        c = self.canonical
+        self.proj = OracleProjection(c.equality_sparsity, c.inequality_sparsity, c.variable_size,
+                                     oracle_config(cfg), partitionable)
+
+    def arrays(self, theta, batch):
+        theta = np.zeros((batch, 0), self.dtype) if theta is None else np.asarray(theta, self.dtype)
+        values, rhs = self.canonical.evaluate(theta)
+        values = np.broadcast_to(values, (batch, values.shape[1])).astype(self.dtype)
+        rhs = np.broadcast_to(rhs, (batch, rhs.shape[1])).astype(self.dtype)
+        return to_ell(self.canonical, values), rhs
+
+    def solve(self, target, theta=None, multipliers_eq=None, multipliers_ineq=None, **kw):
+        target = np.asarray(target, self.dtype)
+        values, rhs = self.arrays(theta, target.shape[0])
+        return self.proj.solve(values, rhs, target, multipliers_eq, multipliers_ineq, **kw)
+
+    def __call__(self, target, theta=None):
+        return self.solve(target, theta)[0]["y"]
+
+    def target_jacobian(self, target, theta=None):
+        """d y_b / d target_b per sample via the oracle's implicit VJP: (B, n, n)."""
+        result, saved = self.solve(target, theta)
+        target = np.asarray(target, self.dtype)
+        batch, n = target.shape
+        jac = np.zeros((batch, n, n), self.dtype)
+        for i in range(n):
+            cot = np.zeros_like(target)
+            cot[:, i] = 1
+            jac[:, i, :] = self.proj.vjp(saved, cot)["target"]
+        return jac
+
+
+def ell_to_csr(ell, row_lengths):
+    """Padded ELL values (B, m, width) -> CSR-slot values (B, nnz)."""
+    parts = [ell[:, i, :k] for i, k in enumerate(row_lengths)]
+    if not parts:
+        return np.zeros((ell.shape[0], 0), ell.dtype)
+    return np.concatenate(parts, axis=1)
+
+
+def random_sparse_problem(rng, n, me, mi, nnz_per_row, bounds=True, lower=-1.0, upper=1.0):
+    """Random ParametricQP-like problem as a canonical Projection with box rows.
+
+    Returns (problem, theta) with theta = [b; h] from a feasible x0.
+    """
+    import scipy.sparse as sp
+    from purin_b200.workloads import _box_qp, _random_rows
+
+    A_eq = _random_rows(rng, me, n, nnz_per_row)
+    A_in = _random_rows(rng, mi, n, nnz_per_row)
+    lo = np.full(n, lower)
+    up = np.full(n, upper)
+    if bounds:
+        problem = _box_qp(A_eq, A_in, lo, up, "random")
+    else:
+        from purin_b200.problems import ParametricQP
+        p = me + mi
+        problem = ParametricQP(
+            P=sp.identity(n), q0=np.zeros(n), A_eq=A_eq, b_eq0=np.zeros(me),
+            b_eq_parameter_map=sp.hstack([sp.identity(me), sp.csr_matrix((me, mi))]).tocsr(),
+            A_ineq=A_in, b_ineq0=np.zeros(mi),
+            b_ineq_parameter_map=sp.hstack([sp.csr_matrix((mi, me)), sp.identity(mi)]).tocsr())
+    return problem, (A_eq, A_in)
+
+
+def random_theta(rng, mats, batch, slack=0.1):
+    A_eq, A_in = mats
+    n = A_eq.shape[1]
+    x0 = rng.uniform(-0.5, 0.5, (batch, n))
+    b = (A_eq @ x0.T).T
+    h = (A_in @ x0.T).T + rng.uniform(0.0, slack, (batch, A_in.shape[0]))
+    return np.concatenate([b, h], axis=1)

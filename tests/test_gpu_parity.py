@@ -1,0 +1,208 @@
+"""CUDA kernels vs the CPU oracle at the C-ABI boundary and through the public API.
+
+Forward results at a fixed iteration count are compared bit for bit (the
+kernels and the oracle perform the same IEEE operations in the same order);
+quantities that involve a parallel sum in the kernel (the normalised gap, the
+power-iteration norm, GMRES dot products) are compared with tolerances.
+"""
+
+import numpy as np
+import pytest
+import torch
+from dataclasses import replace
+
+from helpers import OracleLayer, ell_to_csr, random_sparse_problem, random_theta
+from purin_b200 import ChambollePockConfig, LinearSolverConfig, prepare_projection
+from purin_b200.workloads import make_workload
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _t(a, dtype):
+    return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype, device=DEV)
+
+
+def _layer(problem, cfg, batch, dtype):
+    return prepare_projection(problem, method="chambolle-pock", config=cfg, batch_size=batch,
+                              dtype=dtype, backend=DEV)
+
+
+def boundary_forward(layer, oracle, saved):
+    """Run purin_cp_forward on the oracle's scaled arrays; returns numpy CPOutput fields."""
+    dt = layer._tdtype
+    data = _t(ell_to_csr(saved["values"], list(oracle.proj.mask.sum(axis=1))), dt)
+    batch, n = saved["target"].shape
+    m = layer._m
+    out = dict(y=torch.empty((batch, n), dtype=dt, device=DEV),
+               dual=torch.empty((batch, m), dtype=dt, device=DEV),
+               iterations=torch.empty((batch,), dtype=torch.int32, device=DEV),
+               residual=torch.empty((batch,), dtype=dt, device=DEV),
+               gap=torch.empty((batch,), dtype=dt, device=DEV),
+               converged=torch.empty((batch,), dtype=torch.uint8, device=DEV))
+    layer._forward_native(data, _t(saved["rhs"], dt), _t(saved["target"], dt),
+                          _t(saved["lower"], dt), _t(saved["upper"], dt),
+                          _t(saved["initial"], dt), _t(saved["tolerance"], dt),
+                          _t(saved["feasible"].astype(np.uint8), torch.uint8),
+                          out["y"], out["dual"], out["iterations"], out["residual"], out["gap"],
+                          out["converged"])
+    torch.cuda.synchronize()
+    return {k: v.cpu().numpy() for k, v in out.items()}, data
+
+
+def boundary_adjoint(layer, oracle, saved, cot):
+    dt = layer._tdtype
+    lengths = list(oracle.proj.mask.sum(axis=1))
+    data = _t(ell_to_csr(saved["values"], lengths), dt)
+    out = saved["out"]
+    grads = layer._adjoint_native(
+        data, _t(saved["rhs"], dt), _t(saved["target"], dt), _t(saved["lower"], dt),
+        _t(saved["upper"], dt), _t(out.y, dt), _t(out.dual, dt),
+        _t(out.converged.astype(np.uint8), torch.uint8), _t(cot, dt), need_values=True,
+        need_rhs=True, need_target=True, need_lower=True, need_upper=True)
+    torch.cuda.synchronize()
+    status, lres = layer._last_linear
+    names = ("values", "rhs", "target", "lower", "upper")
+    return ({k: g.cpu().numpy() for k, g in zip(names, grads)}, status.cpu().numpy(),
+            lres.cpu().numpy())
+
+
+FORWARD_CASES = [
+    # (name, workload index, batch, dtype, config overrides)
+    ("config0-fixed-f64", 0, 16, np.float64, {}),
+    ("config0-accel-f64", 0, 16, np.float64, {"accelerated": True}),
+    ("config0-fixed-f32", 0, 16, np.float32, {}),
+    ("config0-diag-f64", 0, 16, np.float64, {"diagonal_preconditioning": True}),
+    ("config0-power-f64", 0, 16, np.float64, {"norm_bound": False}),
+    ("config0-power-f32", 0, 16, np.float32, {"norm_bound": False}),
+    ("config1-accel-f64", 1, 8, np.float64, {"max_iterations": 200}),
+    ("config1-accel-f32", 1, 8, np.float32, {"max_iterations": 200}),
+    ("config0-converge-f64", 0, 16, np.float64, {"tolerance": 1e-4, "max_iterations": 4000}),
+]
+
+
+@pytest.mark.parametrize("name,index,batch,dtype,overrides", FORWARD_CASES,
+                         ids=[c[0] for c in FORWARD_CASES])
+def test_forward_boundary_matches_oracle(name, index, batch, dtype, overrides):
+    w = make_workload(index, batch)
+    cfg = replace(w.config, **overrides)
+    oracle = OracleLayer(w.problem, cfg, dtype)
+    expected, saved = oracle.solve(w.candidates, w.theta)
+    tdt = torch.float64 if dtype == np.float64 else torch.float32
+    layer = _layer(w.problem, cfg, batch, tdt)
+    got, _ = boundary_forward(layer, oracle, saved)
+    out = saved["out"]
+    np.testing.assert_array_equal(got["iterations"], out.iterations)
+    np.testing.assert_array_equal(got["converged"].astype(bool), out.converged)
+    if not overrides.get("norm_bound", True):
+        # tau/sigma come from a parallel-sum power iteration: agree to rounding.
+        tol = 1e-9 if dtype == np.float64 else 2e-3
+        np.testing.assert_allclose(got["y"], out.y, rtol=0, atol=tol)
+        return
+    np.testing.assert_array_equal(got["y"], out.y)
+    np.testing.assert_array_equal(got["dual"], out.dual)
+    np.testing.assert_array_equal(got["residual"], out.residual)
+    rtol = 1e-12 if dtype == np.float64 else 1e-5
+    np.testing.assert_allclose(got["gap"], out.gap, rtol=rtol, atol=rtol)
+
+
+@pytest.mark.parametrize("index,batch,dtype", [(0, 16, np.float64), (1, 4, np.float64),
+                                               (0, 16, np.float32)])
+def test_public_solve_matches_oracle(index, batch, dtype):
+    """End to end: torch preprocessing + forward + post-processing kernels."""
+    w = make_workload(index, batch)
+    cfg = replace(w.config, max_iterations=min(w.config.max_iterations, 300))
+    oracle = OracleLayer(w.problem, cfg, dtype)
+    expected, _ = oracle.solve(w.candidates, w.theta)
+    tdt = torch.float64 if dtype == np.float64 else torch.float32
+    layer = _layer(w.problem, cfg, batch, tdt)
+    got = layer.solve(_t(w.candidates, tdt), _t(w.theta, tdt))
+    np.testing.assert_array_equal(got.y.cpu().numpy(), expected["y"])
+    for field in ("multipliers_eq", "multipliers_ineq", "slacks", "residual_inf_norm"):
+        np.testing.assert_array_equal(getattr(got, field).cpu().numpy(), expected[field],
+                                      err_msg=field)
+    np.testing.assert_array_equal(got.status.cpu().numpy(), expected["status"])
+    np.testing.assert_array_equal(got.iterations.cpu().numpy(), expected["iterations"])
+    np.testing.assert_array_equal(got.finite.cpu().numpy(), expected["finite"])
+    np.testing.assert_array_equal(got.gradient_eligible.cpu().numpy(),
+                                  expected["gradient_eligible"])
+
+
+def _converging_problem(seed, n=8, me=2, mi=4, dtype=np.float64):
+    rng = np.random.default_rng(seed)
+    problem, mats = random_sparse_problem(rng, n, me, mi, 3)
+    batch = 6
+    theta = random_theta(rng, mats, batch)
+    target = 1.5 * rng.normal(size=(batch, n))
+    return problem, theta.astype(dtype), target.astype(dtype)
+
+
+@pytest.mark.parametrize("seed,accelerated", [(1, False), (2, False), (3, False), (1, True),
+                                              (5, True)])
+def test_adjoint_boundary_matches_oracle(seed, accelerated):
+    problem, theta, target = _converging_problem(seed)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-11, accelerated=accelerated)
+    oracle = OracleLayer(problem, cfg)
+    expected, saved = oracle.solve(target, theta)
+    assert expected["gradient_eligible"].any()
+    rng = np.random.default_rng(100 + seed)
+    cot = rng.normal(size=target.shape)
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    layer = _layer(problem, cfg, target.shape[0], torch.float64)
+    got, status, lres = boundary_adjoint(layer, oracle, saved, cot)
+    np.testing.assert_array_equal(status, stats["code"])
+    for key in ("values", "rhs", "target", "lower", "upper"):
+        exp = want[key]
+        if key == "values":
+            exp = ell_to_csr(exp, list(oracle.proj.mask.sum(axis=1)))
+        np.testing.assert_allclose(got[key], exp, rtol=0, atol=1e-9, err_msg=key)
+
+
+def test_adjoint_gmres_budget_matches_oracle():
+    """Hard case: GMRES stops at its iteration budget; residuals agree to rounding."""
+    w = make_workload(0, 6)
+    cfg = replace(w.config, max_iterations=6000, tolerance=1e-5)
+    oracle = OracleLayer(w.problem, cfg)
+    expected, saved = oracle.solve(w.candidates, w.theta)
+    assert expected["gradient_eligible"].any()
+    cot = np.random.default_rng(7).normal(size=w.candidates.shape)
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    layer = _layer(w.problem, cfg, 6, torch.float64)
+    got, status, lres = boundary_adjoint(layer, oracle, saved, cot)
+    np.testing.assert_array_equal(status, stats["code"])
+    np.testing.assert_allclose(lres, stats["residual"], rtol=1e-6, atol=1e-14)
+    for key in ("rhs", "target"):
+        np.testing.assert_allclose(got[key], want[key], rtol=0, atol=1e-9, err_msg=key)
+
+
+def test_autograd_chain_matches_fd():
+    """Public API gradient w.r.t. candidate and parameters vs central differences."""
+    problem, theta, target = _converging_problem(5)
+    cfg = replace(ChambollePockConfig(max_iterations=20000, tolerance=1e-12),
+                  implicit_gradient=replace(ChambollePockConfig().implicit_gradient,
+                                            differentiate_problem_parameters=True),
+                  linear_solver=LinearSolverConfig(tolerance=1e-12))
+    layer = _layer(problem, cfg, target.shape[0], torch.float64)
+    x = _t(target, torch.float64).requires_grad_(True)
+    th = _t(theta, torch.float64).requires_grad_(True)
+    g = torch.as_tensor(np.random.default_rng(9).normal(size=target.shape), device=DEV)
+    result = layer.solve(x, th)
+    assert bool(result.gradient_eligible.all())
+    (result.y * g).sum().backward()
+    eps = 1e-6
+    for which, base, grad in (("x", target, x.grad), ("theta", theta, th.grad)):
+        fd = np.zeros_like(base)
+        for b in range(base.shape[0]):
+            for i in range(base.shape[1]):
+                plus, minus = base.copy(), base.copy()
+                plus[b, i] += eps
+                minus[b, i] -= eps
+                args_p = (plus, theta) if which == "x" else (target, plus)
+                args_m = (minus, theta) if which == "x" else (target, minus)
+                yp = layer(_t(args_p[0], torch.float64), _t(args_p[1], torch.float64))
+                ym = layer(_t(args_m[0], torch.float64), _t(args_m[1], torch.float64))
+                fd[b, i] = float(((yp - ym) * g).sum()) / (2 * eps)
+        np.testing.assert_allclose(grad.cpu().numpy(), fd, atol=2e-6, err_msg=which)
