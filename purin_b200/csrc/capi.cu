@@ -54,15 +54,37 @@ struct FwdPlan {
   int S = 1;
   bool smem = true;
   size_t smem_bytes = 0;
-  size_t workspace = 0;
+  size_t workspace = 0;  // total bytes
+  size_t off_vr = 0, off_vc = 0, off_state = 0;
+  int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
 
+int log2_int(int v) {
+  int r = 0;
+  while ((1 << r) < v) ++r;
+  return r;
+}
+
+FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch);
+
 FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
+  FwdPlan fp = plan_forward_tiles(plan, cfg, batch);
+  const size_t w = dtype_size(plan->info.dtype);
+  fp.sell_index = log2_int(fp.S);
+  const purin::SellView& sv = plan->sell[fp.sell_index];
+  fp.off_vr = 0;
+  fp.off_vc = align_up((size_t)sv.nnz_r * w);
+  fp.off_state = fp.off_vc + align_up((size_t)sv.nnz_c * w);
+  fp.workspace = fp.off_state + fp.workspace;
+  return fp;
+}
+
+FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
   FwdPlan fp;
   const int n = plan->info.n, m = plan->info.kept_rows;
   const size_t w = dtype_size(plan->info.dtype);
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
-  const size_t per_sample = (size_t)(2 * n + m + (diag ? 2 * n + m : 0)) * w;
+  const size_t per_sample = (size_t)(2 * (n + 1) + (m + 1) + (diag ? 2 * (n + 1) + (m + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t target_tiles = 2 * (int64_t)std::max(1, plan->sm_count);
   int best = 0;
@@ -160,8 +182,22 @@ template <typename T>
 int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinCpForwardArgs* a,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   const FwdPlan fp = plan_forward(plan, cfg, a->batch);
-  if (!fp.smem && (workspace == nullptr || workspace_bytes < fp.workspace))
+  if (workspace == nullptr || workspace_bytes < fp.workspace)
     return fail(PURIN_ERR_WORKSPACE, "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes");
+  char* ws = static_cast<char*>(workspace);
+  const purin::SellView& sv = plan->sell[fp.sell_index];
+  // Values shared by the batch are arranged once per call in both sliced-ELL orders.
+  const bool shared = a->values_stride == 0 || a->batch == 1;
+  T* vr = nullptr;
+  T* vc = nullptr;
+  if (shared && plan->info.kept_nnz > 0) {
+    vr = reinterpret_cast<T*>(ws + fp.off_vr);
+    vc = reinterpret_cast<T*>(ws + fp.off_vc);
+    cudaError_t e = purin::arrange_values<T>(static_cast<const T*>(a->values), sv.r_slot, sv.nnz_r, vr, stream);
+    if (e == cudaSuccess)
+      e = purin::arrange_values<T>(static_cast<const T*>(a->values), sv.c_slot, sv.nnz_c, vc, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward value layout");
+  }
   purin::FwdParams<T> p{};
   p.st = plan->dev;
   p.batch = a->batch;
@@ -191,7 +227,10 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.norm_bound = cfg->norm_bound ? 1 : 0;
   p.diag = (cfg->diagonal_preconditioning && !cfg->accelerated) ? 1 : 0;
   p.partitionable = cfg->prng_partitionable ? 1 : 0;
-  p.gstate = fp.smem ? nullptr : static_cast<T*>(workspace);
+  p.gstate = fp.smem ? nullptr : reinterpret_cast<T*>(ws + fp.off_state);
+  p.sell = sv;
+  p.vr = vr;
+  p.vc = vc;
   cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.smem, fp.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward launch");
   return PURIN_OK;
@@ -294,6 +333,44 @@ int32_t run_post(const PurinCpPlan* plan, const PurinCpPostArgs* a, cudaStream_t
   cudaError_t e = purin::launch_post<T>(p, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_postprocess launch");
   return PURIN_OK;
+}
+
+// Sliced-ELL layout (sell.cuh) of `count` lines with entries ptr_in/idx_in and slots
+// slot_in (identity when null), slices of C lines sorted by length (descending, stable).
+struct SellHost {
+  int nsl = 0;
+  std::vector<int32_t> ptr, perm, idx, slot;
+};
+
+SellHost build_sell(int count, const std::vector<int32_t>& ptr_in, const std::vector<int32_t>& idx_in,
+                    const std::vector<int32_t>* slot_in, int C, int pad_index) {
+  SellHost h;
+  std::vector<int32_t> order(count);
+  for (int i = 0; i < count; ++i) order[i] = i;
+  auto len = [&](int i) { return ptr_in[i + 1] - ptr_in[i]; };
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len(a) > len(b); });
+  h.nsl = (count + C - 1) / C;
+  h.perm.assign((size_t)h.nsl * C, -1);
+  for (int q = 0; q < count; ++q) h.perm[q] = order[q];
+  h.ptr.assign(h.nsl + 1, 0);
+  for (int s = 0; s < h.nsl; ++s) h.ptr[s + 1] = h.ptr[s] + len(order[s * C]) * C;
+  h.idx.assign(h.ptr[h.nsl], pad_index);
+  h.slot.assign(h.ptr[h.nsl], -1);
+  for (int s = 0; s < h.nsl; ++s) {
+    const int width = (h.ptr[s + 1] - h.ptr[s]) / C;
+    for (int c = 0; c < C; ++c) {
+      const int q = s * C + c;
+      if (q >= count) continue;
+      const int line = order[q];
+      for (int k = 0; k < len(line) && k < width; ++k) {
+        const int e = h.ptr[s] + k * C + c;
+        const int src = ptr_in[line] + k;
+        h.idx[e] = idx_in[src];
+        h.slot[e] = slot_in ? (*slot_in)[src] : src;
+      }
+    }
+  }
+  return h;
 }
 
 // Counting sort of (row, slot) entries by column, stable in row-major order.
@@ -460,15 +537,68 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
   st.bound_var = d + offsets[14];
   st.var_bound_ptr = d + offsets[15];
   st.var_bound_list = d + offsets[16];
+
+  // Sliced-ELL layouts for every tile width (C = 32 / S).
+  {
+    std::vector<SellHost> layouts;
+    size_t total_sell = 0;
+    for (int q = 0; q < 6; ++q) {
+      const int C = 32 >> q;
+      layouts.push_back(build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n));
+      layouts.push_back(build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows));
+    }
+    for (auto& h : layouts) total_sell += h.ptr.size() + h.perm.size() + 2 * h.idx.size() + 64;
+    std::vector<int32_t> host_sell(total_sell, 0);
+    std::vector<size_t> base;
+    size_t at = 0;
+    for (auto& h : layouts) {
+      base.push_back(at);
+      for (auto* v : {&h.ptr, &h.perm, &h.idx, &h.slot}) {
+        if (!v->empty()) std::memcpy(host_sell.data() + at, v->data(), v->size() * 4);
+        at += v->size() + 16;
+      }
+    }
+    DeviceGuard guard(s->device);
+    cudaError_t e = cudaMalloc(&plan->sell_block, std::max<size_t>(at, 1) * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemcpy(plan->sell_block, host_sell.data(), at * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(plan->device_block);
+      if (plan->sell_block) cudaFree(plan->sell_block);
+      delete plan;
+      return cuda_fail(e, "purin_cp_plan_create (sliced ELL)");
+    }
+    const int32_t* sd = static_cast<const int32_t*>(plan->sell_block);
+    for (int q = 0; q < 6; ++q) {
+      const SellHost& r = layouts[2 * q];
+      const SellHost& c = layouts[2 * q + 1];
+      const int32_t* rb = sd + base[2 * q];
+      const int32_t* cb = sd + base[2 * q + 1];
+      purin::SellView& v = plan->sell[q];
+      v.C = 32 >> q;
+      v.nsl_r = r.nsl;
+      v.nsl_c = c.nsl;
+      v.nnz_r = (int)r.idx.size();
+      v.nnz_c = (int)c.idx.size();
+      v.r_ptr = rb;
+      v.r_perm = rb + r.ptr.size() + 16;
+      v.r_idx = v.r_perm + r.perm.size() + 16;
+      v.r_slot = v.r_idx + r.idx.size() + 16;
+      v.c_ptr = cb;
+      v.c_perm = cb + c.ptr.size() + 16;
+      v.c_idx = v.c_perm + c.perm.size() + 16;
+      v.c_slot = v.c_idx + c.idx.size() + 16;
+    }
+  }
   *out = plan;
   return PURIN_OK;
 }
 
 int32_t purin_cp_plan_destroy(PurinCpPlan* plan) {
   if (!plan) return PURIN_OK;
-  if (plan->device_block) {
+  if (plan->device_block || plan->sell_block) {
     DeviceGuard guard(plan->info.device);
-    cudaFree(plan->device_block);
+    if (plan->device_block) cudaFree(plan->device_block);
+    if (plan->sell_block) cudaFree(plan->sell_block);
   }
   delete plan;
   return PURIN_OK;

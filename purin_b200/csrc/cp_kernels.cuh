@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "plan.cuh"
+#include "sell.cuh"
 
 namespace purin {
 
@@ -40,6 +41,9 @@ struct FwdParams {
   int diag;
   int partitionable;
   T* gstate;  // per-tile state in global memory when it does not fit in shared memory
+  SellView sell;  // sliced-ELL rows/columns for C = 32 / S
+  const T* vr;    // shared values in SELL row order (null: per-sample values via slots)
+  const T* vc;    // shared values in SELL column order
 };
 
 template <typename T>
@@ -127,6 +131,8 @@ cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_
                            cudaStream_t stream);
 template <typename T>
 size_t forward_static_smem(int S);
+template <typename T>
+cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
 
 // Adjoint: shared-memory bytes for one CTA, occupancy-limited cooperative grid.
 template <typename T>

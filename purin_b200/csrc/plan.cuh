@@ -12,6 +12,8 @@
 
 #include <vector>
 
+#include "sell.cuh"
+
 #include "../../include/purin_cp.h"
 
 namespace purin {
@@ -57,4 +59,7 @@ struct PurinCpPlan {
   std::vector<int32_t> kept_row_ptr, kept_cols;
   int sm_count = 0;
   int max_smem_optin = 0;
+  // Sliced-ELL layouts for C = 32, 16, 8, 4, 2, 1 (index log2(32 / C)), built at creation.
+  purin::SellView sell[6];
+  void* sell_block = nullptr;
 };

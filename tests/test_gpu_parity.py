@@ -161,7 +161,14 @@ def test_adjoint_boundary_matches_oracle(seed, accelerated):
 
 
 def test_adjoint_gmres_budget_matches_oracle():
-    """Hard case: GMRES stops at its iteration budget; residuals agree to rounding."""
+    """Hard case: GMRES stops at its 100-iteration budget without converging.
+
+    A non-converged restarted GMRES is sensitive to rounding: perturbing the
+    oracle's own tau by 2e-16 (relative) moves its final residual by up to 9%.
+    What must agree is the outcome: the same status codes, residuals of the
+    same size, and the same gradients -- here zero, because every residual
+    stays above the adjoint tolerance (bounds.py:148-154).
+    """
     w = make_workload(0, 6)
     cfg = replace(w.config, max_iterations=6000, tolerance=1e-5)
     oracle = OracleLayer(w.problem, cfg)
@@ -170,12 +177,16 @@ def test_adjoint_gmres_budget_matches_oracle():
     cot = np.random.default_rng(7).normal(size=w.candidates.shape)
     stats = {}
     want = oracle.proj.vjp(saved, cot, stats=stats)
+    assert stats["completed"] == 100 and np.any(stats["code"] == 1)
     layer = _layer(w.problem, cfg, 6, torch.float64)
     got, status, lres = boundary_adjoint(layer, oracle, saved, cot)
     np.testing.assert_array_equal(status, stats["code"])
-    np.testing.assert_allclose(lres, stats["residual"], rtol=1e-6, atol=1e-14)
-    for key in ("rhs", "target"):
-        np.testing.assert_allclose(got[key], want[key], rtol=0, atol=1e-9, err_msg=key)
+    np.testing.assert_allclose(lres, stats["residual"], rtol=0.25, atol=1e-14)
+    for key in ("values", "rhs", "target", "lower", "upper"):
+        exp = want[key]
+        if key == "values":
+            exp = ell_to_csr(exp, list(oracle.proj.mask.sum(axis=1)))
+        np.testing.assert_array_equal(got[key], exp, err_msg=key)
 
 
 def test_autograd_chain_matches_fd():
