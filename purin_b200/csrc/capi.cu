@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -70,7 +71,7 @@ FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, in
 FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
   FwdPlan fp = plan_forward_tiles(plan, cfg, batch);
   const size_t w = dtype_size(plan->info.dtype);
-  fp.sell_index = log2_int(fp.S);
+  fp.sell_index = 0;  // one lane per line: slices of C = 32 for every tile width
   const purin::SellView& sv = plan->sell[fp.sell_index];
   fp.off_vr = 0;
   fp.off_vc = align_up((size_t)sv.nnz_r * w);
@@ -87,13 +88,23 @@ FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, in
   const size_t per_sample = (size_t)(2 * (n + 1) + (m + 1) + (diag ? 2 * (n + 1) + (m + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t target_tiles = 2 * (int64_t)std::max(1, plan->sm_count);
+  // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it fits.
+  int forced = 0;
+  if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
   int best = 0;
-  for (int S = 1; S <= 32; S *= 2) {
+  for (int S = 1; S <= 8; S *= 2) {
     const size_t stat = plan->info.dtype == PURIN_FLOAT64 ? purin::forward_static_smem<double>(S)
                                                           : purin::forward_static_smem<float>(S);
     if ((size_t)S * per_sample + stat + 1024 > cap) break;
     const int64_t tiles = (batch + S - 1) / S;
-    if (S == 1 || tiles >= target_tiles) best = S;
+    // Default: the widest tile that still leaves room for two CTAs per SM and
+    // gives every SM at least two tiles.
+    const bool two_per_sm = 2 * ((size_t)S * per_sample + stat + 1024) <= cap;
+    if (forced > 0) {
+      if (S <= forced) best = S;
+    } else if (S == 1 || (tiles >= target_tiles && two_per_sm)) {
+      best = S;
+    }
   }
   if (best > 0) {
     fp.S = best;

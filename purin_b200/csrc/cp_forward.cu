@@ -5,11 +5,11 @@
 //
 // One CTA owns a tile of S samples for the whole solve.  The tile's iterates
 // y, ybar (n each) and the duals (m) live in shared memory, interleaved by
-// sample ([element * S + s]) so that a group of S lanes reading one sparse
-// entry (index + value) serves all S samples with a single structure load.
-// The structure is read in the sliced-ELL layout of sell.cuh: a warp owns a
-// slice of C = 32 / S rows (or columns) and reads C consecutive entries per
-// step.  Each iteration makes three passes:
+// sample ([element * S + s]).  The structure is read in the sliced-ELL layout
+// of sell.cuh with C = 32: a warp owns a slice of 32 rows (or columns), each
+// lane one row, and each lane carries that row for all S samples of the tile,
+// so one index load and one value load feed S multiply-adds whose operands
+// arrive as one vector shared-memory load.  Each iteration makes three passes:
 //   A (rows)    lambda+ = proj(lambda + sigma (K ybar - rhs))         kernels.py:133-137
 //   B (columns) t = K.T lambda+, y+ = clip(a y - d t + o), ybar+,
 //               bound violation, primal/dual objective terms, stationarity
@@ -28,8 +28,9 @@ namespace purin {
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kC = 32;  // sliced-ELL slice height: one row per lane
 
 template <typename T, int S>
 struct TileScratch {
@@ -38,90 +39,147 @@ struct TileScratch {
   int active[S], count[S], conv[S];
   T red[kWarps][S][5];
   int redf[kWarps][S];
+  T s_red[kWarps][S];
 };
 
-// Per-sample sum / max over the tile (every thread of sample s receives the total).
+// S consecutive values p[0 .. S-1] with vector loads (16-byte aligned when S * sizeof(T) >= 16).
 template <typename T, int S>
-__device__ __forceinline__ T tile_sum(T v, T* scratch) {
-  v = group_sum<S>(v);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __syncthreads();
-  if (lane < S) scratch[warp * S + lane] = v;
-  __syncthreads();
-  const int s = threadIdx.x % S;
-  T total = T(0);
+__device__ __forceinline__ void load_pack(const T* p, T (&out)[S]) {
+  if constexpr (sizeof(T) * S % 16 == 0) {
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) total = total + scratch[w * S + s];
-  return total;
-}
-template <typename T, int S>
-__device__ __forceinline__ T tile_max(T v, T* scratch) {
-  v = group_max<S>(v);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __syncthreads();
-  if (lane < S) scratch[warp * S + lane] = v;
-  __syncthreads();
-  const int s = threadIdx.x % S;
-  T total = T(0);
+    for (int q = 0; q < S; q += 16 / sizeof(T)) {
+      if constexpr (sizeof(T) == 8) {
+        const double2 t = *reinterpret_cast<const double2*>(p + q);
+        out[q] = t.x;
+        out[q + 1] = t.y;
+      } else {
+        const float4 t = *reinterpret_cast<const float4*>(p + q);
+        out[q] = t.x;
+        out[q + 1] = t.y;
+        out[q + 2] = t.z;
+        out[q + 3] = t.w;
+      }
+    }
+  } else if constexpr (sizeof(T) * S == 8 && sizeof(T) == 4) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    out[0] = t.x;
+    out[1] = t.y;
+  } else {
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) total = pmax(total, scratch[w * S + s]);
-  return total;
+    for (int q = 0; q < S; ++q) out[q] = p[q];
+  }
 }
 
-// Sliced-ELL dot products of one lane group: sum_k value(e) * x[index(e) * S + s].
+// Sliced-ELL accumulation of one lane's line for all S samples:
+// acc[q] += value_q(e) * x[index(e) * S + q] over the line's entries, in order.
 template <typename T, int S, bool kShared>
-struct SellDot {
+struct SellLines {
+  const int* ptr;
+  const int* perm;
   const int* idx;
   const int* slot;
-  const T* sell_vals;  // kShared: values in SELL order
-  const T* vals;       // !kShared: this sample's values in CSR slot order
+  const T* sell_vals;    // kShared: values in SELL order
+  const T* const* vals;  // !kShared: per-sample value rows (CSR slot order)
 
-  __device__ __forceinline__ T value(int e) const {
-    if constexpr (kShared) {
-      return __ldg(sell_vals + e);
-    } else {
-      const int sl = __ldg(slot + e);
-      return sl >= 0 ? vals[sl] : T(0);
+  __device__ __forceinline__ void dot(int sl, int lane, const T* x, T (&acc)[S]) const {
+    const int e0 = __ldg(ptr + sl);
+    const int width = (__ldg(ptr + sl + 1) - e0) / kC;
+#pragma unroll
+    for (int q = 0; q < S; ++q) acc[q] = T(0);
+    int e = e0 + lane;
+#pragma unroll 8
+    for (int k = 0; k < width; ++k, e += kC) {
+      const int col = __ldg(idx + e);
+      T xs[S];
+      load_pack<T, S>(x + (size_t)col * S, xs);
+      if constexpr (kShared) {
+        const T v = __ldg(sell_vals + e);
+#pragma unroll
+        for (int q = 0; q < S; ++q) acc[q] = acc[q] + v * xs[q];
+      } else {
+        const int s0 = __ldg(slot + e);
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const T v = s0 >= 0 ? vals[q][s0] : T(0);
+          acc[q] = acc[q] + v * xs[q];
+        }
+      }
     }
   }
-  __device__ __forceinline__ T dot(int e0, int width, const T* x, int s) const {
-    constexpr int C = 32 / S;
-    T acc = T(0);
-    int e = e0;
-#pragma unroll 4
-    for (int k = 0; k < width; ++k, e += C) acc = acc + value(e) * x[(size_t)__ldg(idx + e) * S + s];
-    return acc;
+  __device__ __forceinline__ void abs_sum(int sl, int lane, T (&acc)[S]) const {
+    const int e0 = __ldg(ptr + sl);
+    const int width = (__ldg(ptr + sl + 1) - e0) / kC;
+#pragma unroll
+    for (int q = 0; q < S; ++q) acc[q] = T(0);
+    int e = e0 + lane;
+    for (int k = 0; k < width; ++k, e += kC) {
+      if constexpr (kShared) {
+        const T v = fabs(__ldg(sell_vals + e)) * T(1);
+#pragma unroll
+        for (int q = 0; q < S; ++q) acc[q] = acc[q] + v;
+      } else {
+        const int s0 = __ldg(slot + e);
+#pragma unroll
+        for (int q = 0; q < S; ++q) acc[q] = acc[q] + fabs(s0 >= 0 ? vals[q][s0] : T(0)) * T(1);
+      }
+    }
   }
-  __device__ __forceinline__ T abs_sum(int e0, int width) const {
-    constexpr int C = 32 / S;
-    T acc = T(0);
-    int e = e0;
-#pragma unroll 4
-    for (int k = 0; k < width; ++k, e += C) acc = acc + fabs(value(e)) * T(1);
-    return acc;
-  }
+  __device__ __forceinline__ int line(int sl, int lane) const { return __ldg(perm + sl * kC + lane); }
 };
 
+template <typename T>
+__device__ __forceinline__ T warp_sum32(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += shfl_xor(v, o);
+  return v;
+}
+template <typename T>
+__device__ __forceinline__ T warp_max32(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = pmax(v, shfl_xor(v, o));
+  return v;
+}
+
+// Per-sample tile reductions; every thread receives all S totals.
+template <typename T, int S, bool kMax>
+__device__ __forceinline__ void tile_reduce(T (&v)[S], T (&scratch)[kWarps][S]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < S; ++q) v[q] = kMax ? warp_max32(v[q]) : warp_sum32(v[q]);
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < S; ++q) scratch[warp][q] = v[q];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    T total = T(0);
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) total = kMax ? pmax(total, scratch[w][q]) : total + scratch[w][q];
+    v[q] = total;
+  }
+}
+
 template <typename T, int S, bool kSmem, bool kShared>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, (S <= 2) ? 2 : 1)
 cp_forward_kernel(const FwdParams<T> p) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
   __shared__ TileScratch<T, S> sc;
-  __shared__ T s_scratch[kWarps * S];
-  constexpr int C = 32 / S;
 
   const DevStructure& st = p.st;
   const SellView& sv = p.sell;
   const int n = st.n, m = st.m, me = st.me;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int s = tid % S;
-  const int g = tid / S;
-  const int gw = lane / S;  // lane group within the warp: position in a slice
-  constexpr int G = kThreads / S;
-  const int64_t b_raw = (int64_t)blockIdx.x * S + s;
-  const bool valid = b_raw < p.batch;
-  const int64_t b = valid ? b_raw : (p.batch - 1);
+
+  // Sample q of this tile (reads of the padding samples of the last tile are clamped).
+  const int64_t tile0 = (int64_t)blockIdx.x * S;
+  auto sample = [&](int q) -> int64_t { return tile0 + q < p.batch ? tile0 + q : p.batch - 1; };
+  auto is_valid = [&](int q) -> bool { return tile0 + q < p.batch; };
+  const T* vals_q[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) vals_q[q] = p.values + sample(q) * p.values_stride;
 
   const size_t tile_elems = (size_t)(2 * (n + 1) + (m + 1) + (p.diag ? 2 * (n + 1) + (m + 1) : 0)) * S;
   T* base = kSmem ? reinterpret_cast<T*>(dyn_smem) : p.gstate + (size_t)blockIdx.x * tile_elems;
@@ -132,260 +190,338 @@ cp_forward_kernel(const FwdParams<T> p) {
   T* dv = av + (size_t)(n + 1) * S;
   T* sv_ = dv + (size_t)(n + 1) * S;
 
-  const T* vals = p.values + b * p.values_stride;
-  const SellDot<T, S, kShared> rows{sv.r_idx, sv.r_slot, p.vr, vals};
-  const SellDot<T, S, kShared> cols{sv.c_idx, sv.c_slot, p.vc, vals};
-  const T* tgt = p.target + b * n;
-  const T* rhs = p.rhs + b * m;
-  const T* lo = p.lower + b * p.bounds_stride;
-  const T* up = p.upper + b * p.bounds_stride;
+  const SellLines<T, S, kShared> rows{sv.r_ptr, sv.r_perm, sv.r_idx, sv.r_slot, p.vr, vals_q};
+  const SellLines<T, S, kShared> cols{sv.c_ptr, sv.c_perm, sv.c_idx, sv.c_slot, p.vc, vals_q};
   const T zero = T(0), one = T(1);
   const T safety = p.safety;
 
-  // Padding elements of the gathered vectors are zero for the whole solve.
-  if (tid < S) {
-    y[(size_t)n * S + s] = zero;
-    ybar[(size_t)n * S + s] = zero;
-    lam[(size_t)m * S + s] = zero;
-  }
-
   // ---- step sizes (kernels.py:209-227) ------------------------------------
-  T L = one;
+  T L[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) L[q] = one;
   if (p.diag) {
     // diagonal_step_sizes (kernels.py:76-88): |K| row and column sums.
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      const int i = __ldg(sv.r_perm + sl * C + gw);
-      const int e0 = __ldg(sv.r_ptr + sl);
-      const T acc = rows.abs_sum(e0 + gw, (__ldg(sv.r_ptr + sl + 1) - e0) / C);
+      T acc[S];
+      rows.abs_sum(sl, lane, acc);
+      const int i = rows.line(sl, lane);
       if (i >= 0) {
-        const T r = acc > zero ? pmax(acc, T(1e-12)) : one;
-        sv_[(size_t)i * S + s] = safety / r;
+#pragma unroll
+        for (int q = 0; q < S; ++q)
+          sv_[(size_t)i * S + q] = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
       }
     }
     for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
-      const int j = __ldg(sv.c_perm + sl * C + gw);
-      const int e0 = __ldg(sv.c_ptr + sl);
-      const T acc = cols.abs_sum(e0 + gw, (__ldg(sv.c_ptr + sl + 1) - e0) / C);
+      T acc[S];
+      cols.abs_sum(sl, lane, acc);
+      const int j = cols.line(sl, lane);
       if (j >= 0) {
-        const T c = acc > zero ? pmax(acc, T(1e-12)) : one;
-        const T tau = safety / c;
-        const T a = one / (one + tau * one);
-        av[(size_t)j * S + s] = a;
-        dv[(size_t)j * S + s] = tau * a;
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const T tau = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
+          const T a = one / (one + tau * one);
+          av[(size_t)j * S + q] = a;
+          dv[(size_t)j * S + q] = tau * a;
+        }
       }
     }
   } else if (p.norm_bound) {
-    T rmax = zero, cmax = zero;
+    T rmax[S], cmax[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) rmax[q] = cmax[q] = zero;
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      const int e0 = __ldg(sv.r_ptr + sl);
-      rmax = pmax(rmax, rows.abs_sum(e0 + gw, (__ldg(sv.r_ptr + sl + 1) - e0) / C));
+      T acc[S];
+      rows.abs_sum(sl, lane, acc);
+#pragma unroll
+      for (int q = 0; q < S; ++q) rmax[q] = pmax(rmax[q], acc[q]);
     }
     for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
-      const int e0 = __ldg(sv.c_ptr + sl);
-      cmax = pmax(cmax, cols.abs_sum(e0 + gw, (__ldg(sv.c_ptr + sl + 1) - e0) / C));
+      T acc[S];
+      cols.abs_sum(sl, lane, acc);
+#pragma unroll
+      for (int q = 0; q < S; ++q) cmax[q] = pmax(cmax[q], acc[q]);
     }
-    rmax = tile_max<T, S>(rmax, s_scratch);
-    cmax = tile_max<T, S>(cmax, s_scratch);
-    L = pmax(sqrt(rmax * cmax), T(1e-12));
+    tile_reduce<T, S, true>(rmax, sc.s_red);
+    tile_reduce<T, S, true>(cmax, sc.s_red);
+#pragma unroll
+    for (int q = 0; q < S; ++q) L[q] = pmax(sqrt(rmax[q] * cmax[q]), T(1e-12));
   } else {
     // norm_estimate (kernels.py:52-65): power iteration on K.T K.
-    uint32_t k0, k1;
-    split_key(p.norm_seed, p.sample_offset + b, p.total_batch, p.partitionable != 0, k0, k1);
     T* x = y;      // n (+ zero pad)
     T* u = lam;    // m (+ zero pad)
-    T* z = ybar;   // n
-    T ss = zero;
-    for (int j = g; j < n; j += G) {
-      const T v = NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0);
-      x[(size_t)j * S + s] = v;
-      ss = ss + v * v;
+    T* z = ybar;   // n (+ zero pad)
+    T ss[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) {
+      uint32_t k0, k1;
+      split_key(p.norm_seed, p.sample_offset + sample(q), p.total_batch, p.partitionable != 0, k0, k1);
+      ss[q] = zero;
+      for (int j = tid; j < n; j += kThreads) {
+        const T v = NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0);
+        x[(size_t)j * S + q] = v;
+        ss[q] = ss[q] + v * v;
+      }
     }
-    const T nrm = sqrt(tile_sum<T, S>(ss, s_scratch)) + T(1e-12);
-    for (int j = g; j < n; j += G) x[(size_t)j * S + s] = x[(size_t)j * S + s] / nrm;
-    T eig = zero;
+    if (tid < S) {
+      x[(size_t)n * S + tid] = zero;
+      u[(size_t)m * S + tid] = zero;
+    }
+    tile_reduce<T, S, false>(ss, sc.s_red);
+    for (int j = tid; j < n; j += kThreads) {
+#pragma unroll
+      for (int q = 0; q < S; ++q) x[(size_t)j * S + q] = x[(size_t)j * S + q] / (sqrt(ss[q]) + T(1e-12));
+    }
+    T eig[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) eig[q] = zero;
     for (int it = 0; it < p.norm_iterations; ++it) {
       __syncthreads();
       for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-        const int i = __ldg(sv.r_perm + sl * C + gw);
-        const int e0 = __ldg(sv.r_ptr + sl);
-        const T acc = rows.dot(e0 + gw, (__ldg(sv.r_ptr + sl + 1) - e0) / C, x, s);
-        if (i >= 0) u[(size_t)i * S + s] = acc;
-      }
-      __syncthreads();
-      T xz = zero, zz = zero;
-      for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
-        const int j = __ldg(sv.c_perm + sl * C + gw);
-        const int e0 = __ldg(sv.c_ptr + sl);
-        const T acc = cols.dot(e0 + gw, (__ldg(sv.c_ptr + sl + 1) - e0) / C, u, s);
-        if (j >= 0) {
-          z[(size_t)j * S + s] = acc;
-          xz = xz + x[(size_t)j * S + s] * acc;
-          zz = zz + acc * acc;
+        T acc[S];
+        rows.dot(sl, lane, x, acc);
+        const int i = rows.line(sl, lane);
+        if (i >= 0) {
+#pragma unroll
+          for (int q = 0; q < S; ++q) u[(size_t)i * S + q] = acc[q];
         }
       }
-      eig = tile_sum<T, S>(xz, s_scratch);
-      const T zn = sqrt(tile_sum<T, S>(zz, s_scratch)) + T(1e-12);
-      for (int j = g; j < n; j += G) x[(size_t)j * S + s] = z[(size_t)j * S + s] / zn;
+      __syncthreads();
+      T xz[S], zz[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) xz[q] = zz[q] = zero;
+      for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
+        T acc[S];
+        cols.dot(sl, lane, u, acc);
+        const int j = cols.line(sl, lane);
+        if (j >= 0) {
+#pragma unroll
+          for (int q = 0; q < S; ++q) {
+            z[(size_t)j * S + q] = acc[q];
+            xz[q] = xz[q] + x[(size_t)j * S + q] * acc[q];
+            zz[q] = zz[q] + acc[q] * acc[q];
+          }
+        }
+      }
+      tile_reduce<T, S, false>(xz, sc.s_red);
+      tile_reduce<T, S, false>(zz, sc.s_red);
+#pragma unroll
+      for (int q = 0; q < S; ++q) eig[q] = xz[q];
+      for (int j = tid; j < n; j += kThreads) {
+#pragma unroll
+        for (int q = 0; q < S; ++q) x[(size_t)j * S + q] = z[(size_t)j * S + q] / (sqrt(zz[q]) + T(1e-12));
+      }
     }
-    L = pmax(sqrt(pmax(eig, zero)) + T(1e-12), T(1e-12));
+#pragma unroll
+    for (int q = 0; q < S; ++q) L[q] = pmax(sqrt(pmax(eig[q], zero)) + T(1e-12), T(1e-12));
     __syncthreads();
   }
 
   // ---- initial state: y = ybar = target, lambda = dual0 --------------------
-  for (int j = g; j < n; j += G) {
-    const T t = tgt[j];
-    y[(size_t)j * S + s] = t;
-    ybar[(size_t)j * S + s] = t;
+  for (int j = tid; j < n; j += kThreads) {
+#pragma unroll
+    for (int q = 0; q < S; ++q) {
+      const T t = p.target[sample(q) * n + j];
+      y[(size_t)j * S + q] = t;
+      ybar[(size_t)j * S + q] = t;
+    }
   }
-  for (int i = g; i < m; i += G) lam[(size_t)i * S + s] = p.dual0 ? p.dual0[b * m + i] : zero;
+  for (int i = tid; i < m; i += kThreads) {
+#pragma unroll
+    for (int q = 0; q < S; ++q) lam[(size_t)i * S + q] = p.dual0 ? p.dual0[sample(q) * m + i] : zero;
+  }
   if (tid < S) {
-    y[(size_t)n * S + s] = zero;
-    ybar[(size_t)n * S + s] = zero;
-    lam[(size_t)m * S + s] = zero;
-    const T tau = p.accelerated ? safety / L : safety / (one + L);
-    sc.tau[s] = tau;
-    sc.sigma[s] = safety / L;
-    sc.theta[s] = one;
-    sc.a[s] = one / (one + tau * one);
-    sc.d[s] = tau * sc.a[s];
-    sc.tol[s] = p.tol[b];
-    sc.active[s] = valid ? 1 : 0;
-    sc.count[s] = 0;
-    sc.conv[s] = 0;
-    sc.res_out[s] = zero;
-    sc.gap_out[s] = zero;
+    const int q = tid;
+    // Padding elements of the gathered vectors stay zero for the whole solve.
+    y[(size_t)n * S + q] = zero;
+    ybar[(size_t)n * S + q] = zero;
+    lam[(size_t)m * S + q] = zero;
+    const T tau = p.accelerated ? safety / L[q] : safety / (one + L[q]);
+    sc.tau[q] = tau;
+    sc.sigma[q] = safety / L[q];
+    sc.theta[q] = one;
+    sc.a[q] = one / (one + tau * one);
+    sc.d[q] = tau * sc.a[q];
+    sc.tol[q] = p.tol[sample(q)];
+    sc.active[q] = is_valid(q) ? 1 : 0;
+    sc.count[q] = 0;
+    sc.conv[q] = 0;
+    sc.res_out[q] = zero;
+    sc.gap_out[q] = zero;
   }
   __syncthreads();
 
-  for (int it = 0; it < p.max_iterations; ++it) {
-    int any = 0;
+  // Warp partials of the per-sample diagnostics: [warp][sample][0..4] =
+  // residual max, stationarity max, primal sum, dual sum, rhs.dual sum.
+  auto publish = [&](int slot, T (&v)[S], bool is_max) {
 #pragma unroll
-    for (int q = 0; q < S; ++q) any |= sc.active[q];
-    if (!any) break;
-    const bool act = sc.active[s] != 0;
-    const T sigma = sc.sigma[s];
-    const T a = sc.a[s], d = sc.d[s], theta = sc.theta[s];
-    int fin = 1;
-    T rd = zero;
-    // Phase A: dual update.
-    for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      const int i = __ldg(sv.r_perm + sl * C + gw);
-      const int e0 = __ldg(sv.r_ptr + sl);
-      const T acc = rows.dot(e0 + gw, (__ldg(sv.r_ptr + sl + 1) - e0) / C, ybar, s);
-      if (i >= 0 && act) {
-        const T sg = p.diag ? sv_[(size_t)i * S + s] : sigma;
-        const T rb = rhs[i];
-        const T raw = lam[(size_t)i * S + s] + sg * (acc - rb);
-        const T nl = i < me ? raw : pmax(raw, zero);
-        lam[(size_t)i * S + s] = nl;
-        fin &= finite(nl) ? 1 : 0;
-        rd = rd + rb * nl;
+    for (int q = 0; q < S; ++q) {
+      const T r = is_max ? warp_max32(v[q]) : warp_sum32(v[q]);
+      if (lane == 0) sc.red[warp][q][slot] = r;
+    }
+  };
+  for (int it = 0; it < p.max_iterations; ++it) {
+    int act = 0;
+#pragma unroll
+    for (int q = 0; q < S; ++q) act |= (sc.active[q] != 0) << q;
+    if (!act) break;
+    int fin = (1 << S) - 1;
+    {
+      // Phase A: dual update.
+      T rd[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) rd[q] = zero;
+      for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
+        T acc[S];
+        const int i = rows.line(sl, lane);
+        // Per-sample operands are loaded before the product so their latency overlaps it.
+        T rbs[S];
+#pragma unroll
+        for (int q = 0; q < S; ++q) rbs[q] = p.rhs[sample(q) * m + (i >= 0 ? i : 0)];
+        rows.dot(sl, lane, ybar, acc);
+        if (i >= 0) {
+#pragma unroll
+          for (int q = 0; q < S; ++q) {
+            if (!((act >> q) & 1)) continue;
+            const T sg = p.diag ? sv_[(size_t)i * S + q] : sc.sigma[q];
+            const T rb = rbs[q];
+            const T raw = lam[(size_t)i * S + q] + sg * (acc[q] - rb);
+            const T nl = i < me ? raw : pmax(raw, zero);
+            lam[(size_t)i * S + q] = nl;
+            if (!finite(nl)) fin &= ~(1 << q);
+            rd[q] = rd[q] + rb * nl;
+          }
+        }
       }
+      publish(4, rd, false);
     }
     __syncthreads();
-    // Phase B: primal update and column diagnostics.
-    T resm = zero, stm = zero, ps = zero, ds = zero;
-    for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
-      const int j = __ldg(sv.c_perm + sl * C + gw);
-      const int e0 = __ldg(sv.c_ptr + sl);
-      const T t = cols.dot(e0 + gw, (__ldg(sv.c_ptr + sl + 1) - e0) / C, lam, s);
-      if (j >= 0 && act) {
-        const size_t js = (size_t)j * S + s;
-        const T yo = y[js];
-        const T c = -tgt[j];
-        const T aa = p.diag ? av[js] : a;
-        const T dd = p.diag ? dv[js] : d;
-        const T off = (-dd) * c;
-        const T yr = (aa * yo - dd * t) + off;
-        const T l = lo[j], u = up[j];
-        const T yn = clip(yr, l, u);
-        y[js] = yn;
-        ybar[js] = yn + theta * (yn - yo);
-        fin &= finite(yn) ? 1 : 0;
-        resm = pmax(resm, pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
-        ps = ps + ((T(0.5) * one * yn) * yn + c * yn);
-        const T tt = c + t;
-        const T mn = clip(-tt / one, l, u);
-        ds = ds + (T(0.5) * one * (mn * mn) + tt * mn);
-        const T inner = (one * yn + c) + t;
-        stm = pmax(stm, fabs(yn - clip(yn - inner, l, u)));
+    T resm[S];
+    {
+      // Phase B: primal update and column diagnostics.
+      T stm[S], ps[S], ds[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) resm[q] = stm[q] = ps[q] = ds[q] = zero;
+      for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
+        T t[S];
+        const int j = cols.line(sl, lane);
+        const int jj = j >= 0 ? j : 0;
+        T tg[S], lb[S], ub[S];
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const int64_t b = sample(q);
+          tg[q] = p.target[b * n + jj];
+          lb[q] = p.lower[b * p.bounds_stride + jj];
+          ub[q] = p.upper[b * p.bounds_stride + jj];
+        }
+        cols.dot(sl, lane, lam, t);
+        if (j >= 0) {
+#pragma unroll
+          for (int q = 0; q < S; ++q) {
+            if (!((act >> q) & 1)) continue;
+            const size_t js = (size_t)j * S + q;
+            const T yo = y[js];
+            const T c = -tg[q];
+            const T aa = p.diag ? av[js] : sc.a[q];
+            const T dd = p.diag ? dv[js] : sc.d[q];
+            const T off = (-dd) * c;
+            const T yr = (aa * yo - dd * t[q]) + off;
+            const T l = lb[q];
+            const T u = ub[q];
+            const T yn = clip(yr, l, u);
+            y[js] = yn;
+            ybar[js] = yn + sc.theta[q] * (yn - yo);
+            if (!finite(yn)) fin &= ~(1 << q);
+            resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
+            ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
+            const T tt = c + t[q];
+            const T mn = clip(-tt / one, l, u);
+            ds[q] = ds[q] + (T(0.5) * one * (mn * mn) + tt * mn);
+            const T inner = (one * yn + c) + t[q];
+            stm[q] = pmax(stm[q], fabs(yn - clip(yn - inner, l, u)));
+          }
+        }
       }
+      publish(1, stm, true);
+      publish(2, ps, false);
+      publish(3, ds, false);
     }
     __syncthreads();
     // Phase C: constraint residuals of y+.
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      const int i = __ldg(sv.r_perm + sl * C + gw);
-      const int e0 = __ldg(sv.r_ptr + sl);
-      const T acc = rows.dot(e0 + gw, (__ldg(sv.r_ptr + sl + 1) - e0) / C, y, s);
-      if (i >= 0 && act) {
-        const T r = acc - rhs[i];
-        resm = pmax(resm, i < me ? fabs(r) : pmax(r, zero));
+      T acc[S];
+      const int i = rows.line(sl, lane);
+      T rbs[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) rbs[q] = p.rhs[sample(q) * m + (i >= 0 ? i : 0)];
+      rows.dot(sl, lane, y, acc);
+      if (i >= 0) {
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          if (!((act >> q) & 1)) continue;
+          const T r = acc[q] - rbs[q];
+          resm[q] = pmax(resm[q], i < me ? fabs(r) : pmax(r, zero));
+        }
       }
     }
-    // Per-sample reduction.
-    resm = group_max<S>(resm);
-    stm = group_max<S>(stm);
-    ps = group_sum<S>(ps);
-    ds = group_sum<S>(ds);
-    rd = group_sum<S>(rd);
-    fin = group_and<S>(fin);
-    if (lane < S) {
-      sc.red[warp][lane][0] = resm;
-      sc.red[warp][lane][1] = stm;
-      sc.red[warp][lane][2] = ps;
-      sc.red[warp][lane][3] = ds;
-      sc.red[warp][lane][4] = rd;
-      sc.redf[warp][lane] = fin;
+    publish(0, resm, true);
+    fin = __reduce_and_sync(kFullMask, (unsigned)fin);
+    if (lane == 0) {
+#pragma unroll
+      for (int q = 0; q < S; ++q) sc.redf[warp][q] = (fin >> q) & 1;
     }
     __syncthreads();
     if (tid < S) {
+      const int q = tid;
       T res = zero, stat = zero, P = zero, Dp = zero, Rd = zero;
       int f = 1;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        res = pmax(res, sc.red[w][tid][0]);
-        stat = pmax(stat, sc.red[w][tid][1]);
-        P = P + sc.red[w][tid][2];
-        Dp = Dp + sc.red[w][tid][3];
-        Rd = Rd + sc.red[w][tid][4];
-        f &= sc.redf[w][tid];
+        res = pmax(res, sc.red[w][q][0]);
+        stat = pmax(stat, sc.red[w][q][1]);
+        P = P + sc.red[w][q][2];
+        Dp = Dp + sc.red[w][q][3];
+        Rd = Rd + sc.red[w][q][4];
+        f &= sc.redf[w][q];
       }
       const T D = Dp - Rd;
       const T gap = pmax(P - D, zero) / pmax(one, pmax(fabs(P), fabs(D)));
       const bool finite_all = f && finite(gap);
-      const T tol = sc.tol[tid];
+      const T tol = sc.tol[q];
       const bool accepted = finite_all && res <= tol && gap <= tol && stat <= tol;
-      if (sc.active[tid]) {
-        sc.count[tid] += 1;
-        sc.res_out[tid] = pmax(res, stat);
-        sc.gap_out[tid] = gap;
-        sc.conv[tid] = accepted ? 1 : 0;
-        if (accepted) sc.active[tid] = 0;
+      if (sc.active[q]) {
+        sc.count[q] += 1;
+        sc.res_out[q] = pmax(res, stat);
+        sc.gap_out[q] = gap;
+        sc.conv[q] = accepted ? 1 : 0;
+        if (accepted) sc.active[q] = 0;
       }
       if (p.accelerated) {
-        const T tau = sc.tau[tid];
+        const T tau = sc.tau[q];
         const T nt = one / sqrt(one + one * tau);
         const T ntau = nt * tau;
-        sc.tau[tid] = ntau;
-        sc.sigma[tid] = sc.sigma[tid] / nt;
-        sc.theta[tid] = nt;
-        sc.a[tid] = one / (one + ntau * one);
-        sc.d[tid] = ntau * sc.a[tid];
+        sc.tau[q] = ntau;
+        sc.sigma[q] = sc.sigma[q] / nt;
+        sc.theta[q] = nt;
+        sc.a[q] = one / (one + ntau * one);
+        sc.d[q] = ntau * sc.a[q];
       }
     }
     __syncthreads();
   }
 
   // ---- outputs --------------------------------------------------------------
-  if (valid) {
-    for (int j = g; j < n; j += G) p.y_out[b * n + j] = y[(size_t)j * S + s];
-    for (int i = g; i < m; i += G) p.dual_out[b * m + i] = lam[(size_t)i * S + s];
-    if (g == 0) {
-      p.it_out[b] = sc.count[s];
-      p.res_out[b] = sc.res_out[s];
-      p.gap_out[b] = sc.gap_out[s];
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    if (!is_valid(q)) continue;
+    const int64_t b = sample(q);
+    for (int j = tid; j < n; j += kThreads) p.y_out[b * n + j] = y[(size_t)j * S + q];
+    for (int i = tid; i < m; i += kThreads) p.dual_out[b * m + i] = lam[(size_t)i * S + q];
+    if (tid == 0) {
+      p.it_out[b] = sc.count[q];
+      p.res_out[b] = sc.res_out[q];
+      p.gap_out[b] = sc.gap_out[q];
       const bool feas = p.feasible ? (p.feasible[b] != 0) : true;
-      p.conv_out[b] = (sc.conv[s] && feas) ? 1 : 0;
+      p.conv_out[b] = (sc.conv[q] && feas) ? 1 : 0;
     }
   }
 }
@@ -422,8 +558,6 @@ cudaError_t launch_shared(const FwdParams<T>& p, int S, bool smem, size_t smem_b
     case 2: return launch_s<T, 2, kShared>(p, smem, smem_bytes, stream);
     case 4: return launch_s<T, 4, kShared>(p, smem, smem_bytes, stream);
     case 8: return launch_s<T, 8, kShared>(p, smem, smem_bytes, stream);
-    case 16: return launch_s<T, 16, kShared>(p, smem, smem_bytes, stream);
-    case 32: return launch_s<T, 32, kShared>(p, smem, smem_bytes, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -433,12 +567,10 @@ cudaError_t launch_shared(const FwdParams<T>& p, int S, bool smem, size_t smem_b
 template <typename T>
 size_t forward_static_smem(int S) {
   switch (S) {
-    case 1: return sizeof(TileScratch<T, 1>) + kWarps * 1 * sizeof(T);
-    case 2: return sizeof(TileScratch<T, 2>) + kWarps * 2 * sizeof(T);
-    case 4: return sizeof(TileScratch<T, 4>) + kWarps * 4 * sizeof(T);
-    case 8: return sizeof(TileScratch<T, 8>) + kWarps * 8 * sizeof(T);
-    case 16: return sizeof(TileScratch<T, 16>) + kWarps * 16 * sizeof(T);
-    default: return sizeof(TileScratch<T, 32>) + kWarps * 32 * sizeof(T);
+    case 1: return sizeof(TileScratch<T, 1>);
+    case 2: return sizeof(TileScratch<T, 2>);
+    case 4: return sizeof(TileScratch<T, 4>);
+    default: return sizeof(TileScratch<T, 8>);
   }
 }
 
