@@ -232,6 +232,27 @@ int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config,
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args,
                              void* stream);
 
+/* purin_cp_forward_noalloc: the forward solve of purin_cp_forward for callers
+ * that cannot allocate device memory -- a plugin or custom-call hook that is
+ * given only its input and output buffers, a framework that has reserved
+ * almost all device memory for its own allocator, or a loop where allocation
+ * is not allowed.  It has no counterpart in the reference.
+ *
+ * The scratch that purin_cp_forward takes as `workspace` lives instead in one
+ * fixed device array of PURIN_CP_NOALLOC_SCRATCH_BYTES inside the library
+ * (one copy on every GPU that loads the library, kept until the process
+ * exits).  The call allocates nothing; inputs and outputs are the caller's, as
+ * for purin_cp_forward, and results are identical.  Problems whose scratch
+ * (purin_cp_workspace_size with PURIN_CP_OP_FORWARD) exceeds the array are
+ * rejected with PURIN_ERR_WORKSPACE.  The first call on a device looks up the
+ * array's device address with that device current; make that first call
+ * before any stream capture.  All calls on a device share the one array, so
+ * calls whose executions overlap on the GPU (other streams, other host
+ * threads) race: serialise them. */
+#define PURIN_CP_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int32_t purin_cp_forward_noalloc(const PurinCpPlan* plan, const PurinCpConfig* config,
+                                 const PurinCpForwardArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

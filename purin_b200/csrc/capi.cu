@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -734,3 +735,61 @@ int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* arg
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Forward solve without caller-provided scratch.
+//
+// Some callers cannot allocate device memory on their own: a plugin or custom-
+// call hook that is handed only its input and output buffers, a host framework
+// that has already reserved nearly all device memory for its own allocator, or
+// a latency-critical loop that forbids allocation.  For them the scratch that
+// purin_cp_forward takes from the caller (the batch-shared constraint values
+// in sliced-ELL order and, for problems too large for shared memory, the tile
+// state) lives in one fixed file-scope device array instead.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = PURIN_CP_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocMaxDevices = 128;
+
+// One copy per device that loads this library, held until the process exits.
+// Host code must not use this name as an address: it only stands in for the
+// device array, so the device address is looked up once per device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+}  // namespace
+
+extern "C" int32_t purin_cp_forward_noalloc(const PurinCpPlan* plan, const PurinCpConfig* config,
+                                            const PurinCpForwardArgs* args, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch <= 0) return purin_cp_forward(plan, config, args, nullptr, 0, stream);
+  const int device = plan->info.device;
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(PURIN_ERR_UNSUPPORTED, "purin_cp_forward_noalloc supports device ordinals below 128");
+  const size_t need = plan_forward(plan, config, args->batch).workspace;
+  if (need > kNoAllocScratchBytes)
+    return fail(PURIN_ERR_WORKSPACE,
+                "purin_cp_forward_noalloc needs " + std::to_string(need) +
+                    " bytes of scratch but its fixed device array holds " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    " bytes; use purin_cp_forward with a caller-provided workspace");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    scratch = g_noalloc_address[device];
+    if (scratch == nullptr) {
+      DeviceGuard guard(device);
+      if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+      cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward_noalloc cudaGetSymbolAddress");
+      g_noalloc_address[device] = scratch;
+    }
+  }
+  // Every part of the scratch this solve reads is written earlier in the same
+  // solve, so nothing has to be cleared between calls.
+  return purin_cp_forward(plan, config, args, scratch, kNoAllocScratchBytes, stream);
+}
