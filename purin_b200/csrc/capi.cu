@@ -58,14 +58,9 @@ struct FwdPlan {
   size_t smem_bytes = 0;
   size_t workspace = 0;  // total bytes
   size_t off_vr = 0, off_vc = 0, off_state = 0;
+  size_t off_tgt = 0, off_rhs = 0, off_dual0 = 0, off_lo = 0, off_up = 0;
   int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
-
-int log2_int(int v) {
-  int r = 0;
-  while ((1 << r) < v) ++r;
-  return r;
-}
 
 FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch);
 
@@ -74,9 +69,17 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t w = dtype_size(plan->info.dtype);
   fp.sell_index = 0;  // one lane per line: slices of C = 32 for every tile width
   const purin::SellView& sv = plan->sell[fp.sell_index];
+  // Workspace: shared values in both sliced-ELL orders, then the per-sample inputs
+  // permuted into the internal orders, then (if needed) the global tile state.
+  const size_t nb = (size_t)std::max<int64_t>(batch, 0);
   fp.off_vr = 0;
   fp.off_vc = align_up((size_t)sv.nnz_r * w);
-  fp.off_state = fp.off_vc + align_up((size_t)sv.nnz_c * w);
+  fp.off_tgt = fp.off_vc + align_up((size_t)sv.nnz_c * w);
+  fp.off_rhs = fp.off_tgt + align_up(nb * sv.n_pos * w);
+  fp.off_dual0 = fp.off_rhs + align_up(nb * sv.m_pos * w);
+  fp.off_lo = fp.off_dual0 + align_up(nb * sv.m_pos * w);
+  fp.off_up = fp.off_lo + align_up(nb * sv.n_pos * w);
+  fp.off_state = fp.off_up + align_up(nb * sv.n_pos * w);
   fp.workspace = fp.off_state + fp.workspace;
   return fp;
 }
@@ -86,7 +89,11 @@ FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, in
   const int n = plan->info.n, m = plan->info.kept_rows;
   const size_t w = dtype_size(plan->info.dtype);
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
-  const size_t per_sample = (size_t)(2 * (n + 1) + (m + 1) + (diag ? 2 * (n + 1) + (m + 1) : 0)) * w;
+  (void)n;
+  (void)m;
+  const int n_pos = plan->sell[0].n_pos, m_pos = plan->sell[0].m_pos;
+  const size_t per_sample =
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t target_tiles = 2 * (int64_t)std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it fits.
@@ -210,7 +217,40 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
       e = purin::arrange_values<T>(static_cast<const T*>(a->values), sv.c_slot, sv.nnz_c, vc, stream);
     if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward value layout");
   }
+  // Per-sample inputs in the internal row/column orders (coalesced per-iteration reads).
+  T* tgt_i = reinterpret_cast<T*>(ws + fp.off_tgt);
+  T* rhs_i = reinterpret_cast<T*>(ws + fp.off_rhs);
+  T* dual0_i = a->dual0 ? reinterpret_cast<T*>(ws + fp.off_dual0) : nullptr;
+  T* lo_i = reinterpret_cast<T*>(ws + fp.off_lo);
+  T* up_i = reinterpret_cast<T*>(ws + fp.off_up);
+  const int64_t bound_rows = a->bounds_stride == 0 ? 1 : a->batch;
+  {
+    const int n = plan->info.n, m = plan->info.kept_rows;
+    cudaError_t e = purin::permute_rows<T>(static_cast<const T*>(a->target), n, sv.c_perm, sv.n_pos,
+                                           a->batch, tgt_i, stream);
+    if (e == cudaSuccess && m > 0)
+      e = purin::permute_rows<T>(static_cast<const T*>(a->rhs), m, sv.r_perm, sv.m_pos, a->batch,
+                                 rhs_i, stream);
+    if (e == cudaSuccess && m == 0)
+      e = cudaMemsetAsync(rhs_i, 0, (size_t)a->batch * sv.m_pos * sizeof(T), stream);
+    if (e == cudaSuccess && dual0_i && m > 0)
+      e = purin::permute_rows<T>(static_cast<const T*>(a->dual0), m, sv.r_perm, sv.m_pos, a->batch,
+                                 dual0_i, stream);
+    if (e == cudaSuccess)
+      e = purin::permute_rows<T>(static_cast<const T*>(a->lower), a->bounds_stride, sv.c_perm,
+                                 sv.n_pos, bound_rows, lo_i, stream);
+    if (e == cudaSuccess)
+      e = purin::permute_rows<T>(static_cast<const T*>(a->upper), a->bounds_stride, sv.c_perm,
+                                 sv.n_pos, bound_rows, up_i, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward input layout");
+  }
   purin::FwdParams<T> p{};
+  p.tgt_i = tgt_i;
+  p.rhs_i = rhs_i;
+  p.dual0_i = (dual0_i && plan->info.kept_rows > 0) ? dual0_i : nullptr;
+  p.lo_i = lo_i;
+  p.up_i = up_i;
+  p.bstride_i = a->bounds_stride == 0 ? 0 : plan->sell[0].n_pos;
   p.st = plan->dev;
   p.batch = a->batch;
   p.values = static_cast<const T*>(a->values);
@@ -550,15 +590,23 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
   st.var_bound_ptr = d + offsets[15];
   st.var_bound_list = d + offsets[16];
 
-  // Sliced-ELL layouts for every tile width (C = 32 / S).
+  // Sliced-ELL layout (C = 32) in the internal row/column orders.
   {
     std::vector<SellHost> layouts;
     size_t total_sell = 0;
-    for (int q = 0; q < 6; ++q) {
-      const int C = 32 >> q;
-      layouts.push_back(build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n));
-      layouts.push_back(build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows));
-    }
+    const int C = 32;
+    SellHost rows_h = build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n);
+    SellHost cols_h = build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows);
+    const int m_pos = rows_h.nsl * C, n_pos = cols_h.nsl * C;
+    std::vector<int32_t> pos_of_col(n + 1, n_pos), pos_of_row(info.kept_rows + 1, m_pos);
+    for (int p = 0; p < n_pos; ++p)
+      if (cols_h.perm[p] >= 0) pos_of_col[cols_h.perm[p]] = p;
+    for (int q = 0; q < m_pos; ++q)
+      if (rows_h.perm[q] >= 0) pos_of_row[rows_h.perm[q]] = q;
+    for (auto& v : rows_h.idx) v = pos_of_col[v];  // padding index n -> n_pos
+    for (auto& v : cols_h.idx) v = pos_of_row[v];  // padding index m -> m_pos
+    layouts.push_back(std::move(rows_h));
+    layouts.push_back(std::move(cols_h));
     for (auto& h : layouts) total_sell += h.ptr.size() + h.perm.size() + 2 * h.idx.size() + 64;
     std::vector<int32_t> host_sell(total_sell, 0);
     std::vector<size_t> base;
@@ -580,13 +628,15 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
       return cuda_fail(e, "purin_cp_plan_create (sliced ELL)");
     }
     const int32_t* sd = static_cast<const int32_t*>(plan->sell_block);
-    for (int q = 0; q < 6; ++q) {
-      const SellHost& r = layouts[2 * q];
-      const SellHost& c = layouts[2 * q + 1];
-      const int32_t* rb = sd + base[2 * q];
-      const int32_t* cb = sd + base[2 * q + 1];
-      purin::SellView& v = plan->sell[q];
-      v.C = 32 >> q;
+    {
+      const SellHost& r = layouts[0];
+      const SellHost& c = layouts[1];
+      const int32_t* rb = sd + base[0];
+      const int32_t* cb = sd + base[1];
+      purin::SellView& v = plan->sell[0];
+      v.C = C;
+      v.m_pos = m_pos;
+      v.n_pos = n_pos;
       v.nsl_r = r.nsl;
       v.nsl_c = c.nsl;
       v.nnz_r = (int)r.idx.size();

@@ -5,11 +5,13 @@
 //
 // One CTA owns a tile of S samples for the whole solve.  The tile's iterates
 // y, ybar (n each) and the duals (m) live in shared memory, interleaved by
-// sample ([element * S + s]).  The structure is read in the sliced-ELL layout
-// of sell.cuh with C = 32: a warp owns a slice of 32 rows (or columns), each
-// lane one row, and each lane carries that row for all S samples of the tile,
-// so one index load and one value load feed S multiply-adds whose operands
-// arrive as one vector shared-memory load.  Each iteration makes three passes:
+// sample ([position * S + s]) in the internal row/column orders of sell.cuh,
+// into which the per-sample inputs are permuted before the launch (outputs
+// are scattered back at the end).  The structure is read in the sliced-ELL
+// layout with C = 32: a warp owns a slice of 32 rows (or columns), each lane
+// one line, and each lane carries that line for all S samples of the tile, so
+// one index load and one value load feed S multiply-adds whose operands arrive
+// as one vector shared-memory load.  Each iteration makes three passes:
 //   A (rows)    lambda+ = proj(lambda + sigma (K ybar - rhs))         kernels.py:133-137
 //   B (columns) t = K.T lambda+, y+ = clip(a y - d t + o), ybar+,
 //               bound violation, primal/dual objective terms, stationarity
@@ -161,6 +163,25 @@ __device__ __forceinline__ void tile_reduce(T (&v)[S], T (&scratch)[kWarps][S]) 
   }
 }
 
+template <typename T, int S>
+__device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
+  if constexpr (sizeof(T) * S % 16 == 0) {
+#pragma unroll
+    for (int q = 0; q < S; q += 16 / sizeof(T)) {
+      if constexpr (sizeof(T) == 8) {
+        *reinterpret_cast<double2*>(p + q) = make_double2(v[q], v[q + 1]);
+      } else {
+        *reinterpret_cast<float4*>(p + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      }
+    }
+  } else if constexpr (sizeof(T) * S == 8 && sizeof(T) == 4) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < S; ++q) p[q] = v[q];
+  }
+}
+
 template <typename T, int S, bool kSmem, bool kShared>
 __global__ void __launch_bounds__(kThreads, (S <= 2) ? 2 : 1)
 cp_forward_kernel(const FwdParams<T> p) {
@@ -170,6 +191,7 @@ cp_forward_kernel(const FwdParams<T> p) {
   const DevStructure& st = p.st;
   const SellView& sv = p.sell;
   const int n = st.n, m = st.m, me = st.me;
+  const int n_pos = sv.n_pos, m_pos = sv.m_pos;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
 
@@ -181,14 +203,17 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
   for (int q = 0; q < S; ++q) vals_q[q] = p.values + sample(q) * p.values_stride;
 
-  const size_t tile_elems = (size_t)(2 * (n + 1) + (m + 1) + (p.diag ? 2 * (n + 1) + (m + 1) : 0)) * S;
+  // Iterates in internal positions: y, ybar (n_pos + 1), duals (m_pos + 1); the
+  // last element of each is the zero that padding entries gather.
+  const size_t tile_elems =
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (p.diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * S;
   T* base = kSmem ? reinterpret_cast<T*>(dyn_smem) : p.gstate + (size_t)blockIdx.x * tile_elems;
   T* y = base;
-  T* ybar = y + (size_t)(n + 1) * S;
-  T* lam = ybar + (size_t)(n + 1) * S;
-  T* av = lam + (size_t)(m + 1) * S;  // diagonal steps (only when p.diag)
-  T* dv = av + (size_t)(n + 1) * S;
-  T* sv_ = dv + (size_t)(n + 1) * S;
+  T* ybar = y + (size_t)(n_pos + 1) * S;
+  T* lam = ybar + (size_t)(n_pos + 1) * S;
+  T* av = lam + (size_t)(m_pos + 1) * S;  // diagonal steps (only when p.diag)
+  T* dv = av + (size_t)(n_pos + 1) * S;
+  T* sv_ = dv + (size_t)(n_pos + 1) * S;
 
   const SellLines<T, S, kShared> rows{sv.r_ptr, sv.r_perm, sv.r_idx, sv.r_slot, p.vr, vals_q};
   const SellLines<T, S, kShared> cols{sv.c_ptr, sv.c_perm, sv.c_idx, sv.c_slot, p.vc, vals_q};
@@ -204,25 +229,21 @@ cp_forward_kernel(const FwdParams<T> p) {
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
       T acc[S];
       rows.abs_sum(sl, lane, acc);
-      const int i = rows.line(sl, lane);
-      if (i >= 0) {
+      const int qp = sl * kC + lane;
 #pragma unroll
-        for (int q = 0; q < S; ++q)
-          sv_[(size_t)i * S + q] = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
-      }
+      for (int q = 0; q < S; ++q)
+        sv_[(size_t)qp * S + q] = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
     }
     for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
       T acc[S];
       cols.abs_sum(sl, lane, acc);
-      const int j = cols.line(sl, lane);
-      if (j >= 0) {
+      const int pp = sl * kC + lane;
 #pragma unroll
-        for (int q = 0; q < S; ++q) {
-          const T tau = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
-          const T a = one / (one + tau * one);
-          av[(size_t)j * S + q] = a;
-          dv[(size_t)j * S + q] = tau * a;
-        }
+      for (int q = 0; q < S; ++q) {
+        const T tau = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
+        const T a = one / (one + tau * one);
+        av[(size_t)pp * S + q] = a;
+        dv[(size_t)pp * S + q] = tau * a;
       }
     }
   } else if (p.norm_bound) {
@@ -247,29 +268,30 @@ cp_forward_kernel(const FwdParams<T> p) {
     for (int q = 0; q < S; ++q) L[q] = pmax(sqrt(rmax[q] * cmax[q]), T(1e-12));
   } else {
     // norm_estimate (kernels.py:52-65): power iteration on K.T K.
-    T* x = y;      // n (+ zero pad)
-    T* u = lam;    // m (+ zero pad)
-    T* z = ybar;   // n (+ zero pad)
+    T* x = y;      // n_pos (+ zero pad)
+    T* u = lam;    // m_pos (+ zero pad)
+    T* z = ybar;   // n_pos (+ zero pad)
     T ss[S];
 #pragma unroll
     for (int q = 0; q < S; ++q) {
       uint32_t k0, k1;
       split_key(p.norm_seed, p.sample_offset + sample(q), p.total_batch, p.partitionable != 0, k0, k1);
       ss[q] = zero;
-      for (int j = tid; j < n; j += kThreads) {
-        const T v = NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0);
-        x[(size_t)j * S + q] = v;
+      for (int pp = tid; pp < n_pos; pp += kThreads) {
+        const int j = __ldg(sv.c_perm + pp);
+        const T v = j >= 0 ? NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0) : zero;
+        x[(size_t)pp * S + q] = v;
         ss[q] = ss[q] + v * v;
       }
     }
     if (tid < S) {
-      x[(size_t)n * S + tid] = zero;
-      u[(size_t)m * S + tid] = zero;
+      x[(size_t)n_pos * S + tid] = zero;
+      u[(size_t)m_pos * S + tid] = zero;
     }
     tile_reduce<T, S, false>(ss, sc.s_red);
-    for (int j = tid; j < n; j += kThreads) {
+    for (int pp = tid; pp < n_pos; pp += kThreads) {
 #pragma unroll
-      for (int q = 0; q < S; ++q) x[(size_t)j * S + q] = x[(size_t)j * S + q] / (sqrt(ss[q]) + T(1e-12));
+      for (int q = 0; q < S; ++q) x[(size_t)pp * S + q] = x[(size_t)pp * S + q] / (sqrt(ss[q]) + T(1e-12));
     }
     T eig[S];
 #pragma unroll
@@ -279,11 +301,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
         T acc[S];
         rows.dot(sl, lane, x, acc);
-        const int i = rows.line(sl, lane);
-        if (i >= 0) {
-#pragma unroll
-          for (int q = 0; q < S; ++q) u[(size_t)i * S + q] = acc[q];
-        }
+        store_pack<T, S>(u + (size_t)(sl * kC + lane) * S, acc);
       }
       __syncthreads();
       T xz[S], zz[S];
@@ -292,23 +310,21 @@ cp_forward_kernel(const FwdParams<T> p) {
       for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
         T acc[S];
         cols.dot(sl, lane, u, acc);
-        const int j = cols.line(sl, lane);
-        if (j >= 0) {
+        const size_t pp = (size_t)(sl * kC + lane) * S;
+        store_pack<T, S>(z + pp, acc);
 #pragma unroll
-          for (int q = 0; q < S; ++q) {
-            z[(size_t)j * S + q] = acc[q];
-            xz[q] = xz[q] + x[(size_t)j * S + q] * acc[q];
-            zz[q] = zz[q] + acc[q] * acc[q];
-          }
+        for (int q = 0; q < S; ++q) {
+          xz[q] = xz[q] + x[pp + q] * acc[q];
+          zz[q] = zz[q] + acc[q] * acc[q];
         }
       }
       tile_reduce<T, S, false>(xz, sc.s_red);
       tile_reduce<T, S, false>(zz, sc.s_red);
 #pragma unroll
       for (int q = 0; q < S; ++q) eig[q] = xz[q];
-      for (int j = tid; j < n; j += kThreads) {
+      for (int pp = tid; pp < n_pos; pp += kThreads) {
 #pragma unroll
-        for (int q = 0; q < S; ++q) x[(size_t)j * S + q] = z[(size_t)j * S + q] / (sqrt(zz[q]) + T(1e-12));
+        for (int q = 0; q < S; ++q) x[(size_t)pp * S + q] = z[(size_t)pp * S + q] / (sqrt(zz[q]) + T(1e-12));
       }
     }
 #pragma unroll
@@ -317,24 +333,25 @@ cp_forward_kernel(const FwdParams<T> p) {
   }
 
   // ---- initial state: y = ybar = target, lambda = dual0 --------------------
-  for (int j = tid; j < n; j += kThreads) {
+  for (int pp = tid; pp < n_pos; pp += kThreads) {
+    T t[S];
 #pragma unroll
-    for (int q = 0; q < S; ++q) {
-      const T t = p.target[sample(q) * n + j];
-      y[(size_t)j * S + q] = t;
-      ybar[(size_t)j * S + q] = t;
-    }
+    for (int q = 0; q < S; ++q) t[q] = p.tgt_i[sample(q) * n_pos + pp];
+    store_pack<T, S>(y + (size_t)pp * S, t);
+    store_pack<T, S>(ybar + (size_t)pp * S, t);
   }
-  for (int i = tid; i < m; i += kThreads) {
+  for (int qp = tid; qp < m_pos; qp += kThreads) {
+    T d0[S];
 #pragma unroll
-    for (int q = 0; q < S; ++q) lam[(size_t)i * S + q] = p.dual0 ? p.dual0[sample(q) * m + i] : zero;
+    for (int q = 0; q < S; ++q) d0[q] = p.dual0_i ? p.dual0_i[sample(q) * m_pos + qp] : zero;
+    store_pack<T, S>(lam + (size_t)qp * S, d0);
   }
   if (tid < S) {
     const int q = tid;
     // Padding elements of the gathered vectors stay zero for the whole solve.
-    y[(size_t)n * S + q] = zero;
-    ybar[(size_t)n * S + q] = zero;
-    lam[(size_t)m * S + q] = zero;
+    y[(size_t)n_pos * S + q] = zero;
+    ybar[(size_t)n_pos * S + q] = zero;
+    lam[(size_t)m_pos * S + q] = zero;
     const T tau = p.accelerated ? safety / L[q] : safety / (one + L[q]);
     sc.tau[q] = tau;
     sc.sigma[q] = safety / L[q];
@@ -371,25 +388,28 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
       for (int q = 0; q < S; ++q) rd[q] = zero;
       for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-        T acc[S];
         const int i = rows.line(sl, lane);
+        const int qp = sl * kC + lane;
         // Per-sample operands are loaded before the product so their latency overlaps it.
         T rbs[S];
 #pragma unroll
-        for (int q = 0; q < S; ++q) rbs[q] = p.rhs[sample(q) * m + (i >= 0 ? i : 0)];
+        for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
+        T acc[S];
         rows.dot(sl, lane, ybar, acc);
         if (i >= 0) {
+          T lv[S];
+          load_pack<T, S>(lam + (size_t)qp * S, lv);
 #pragma unroll
           for (int q = 0; q < S; ++q) {
             if (!((act >> q) & 1)) continue;
-            const T sg = p.diag ? sv_[(size_t)i * S + q] : sc.sigma[q];
-            const T rb = rbs[q];
-            const T raw = lam[(size_t)i * S + q] + sg * (acc[q] - rb);
+            const T sg = p.diag ? sv_[(size_t)qp * S + q] : sc.sigma[q];
+            const T raw = lv[q] + sg * (acc[q] - rbs[q]);
             const T nl = i < me ? raw : pmax(raw, zero);
-            lam[(size_t)i * S + q] = nl;
+            lv[q] = nl;
             if (!finite(nl)) fin &= ~(1 << q);
-            rd[q] = rd[q] + rb * nl;
+            rd[q] = rd[q] + rbs[q] * nl;
           }
+          store_pack<T, S>(lam + (size_t)qp * S, lv);
         }
       }
       publish(4, rd, false);
@@ -402,24 +422,27 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
       for (int q = 0; q < S; ++q) resm[q] = stm[q] = ps[q] = ds[q] = zero;
       for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
-        T t[S];
         const int j = cols.line(sl, lane);
-        const int jj = j >= 0 ? j : 0;
+        const int pp = sl * kC + lane;
         T tg[S], lb[S], ub[S];
 #pragma unroll
         for (int q = 0; q < S; ++q) {
           const int64_t b = sample(q);
-          tg[q] = p.target[b * n + jj];
-          lb[q] = p.lower[b * p.bounds_stride + jj];
-          ub[q] = p.upper[b * p.bounds_stride + jj];
+          tg[q] = p.tgt_i[b * n_pos + pp];
+          lb[q] = p.lo_i[b * p.bstride_i + pp];
+          ub[q] = p.up_i[b * p.bstride_i + pp];
         }
+        T t[S];
         cols.dot(sl, lane, lam, t);
         if (j >= 0) {
+          T yv[S], bv[S];
+          load_pack<T, S>(y + (size_t)pp * S, yv);
+          load_pack<T, S>(ybar + (size_t)pp * S, bv);
 #pragma unroll
           for (int q = 0; q < S; ++q) {
             if (!((act >> q) & 1)) continue;
-            const size_t js = (size_t)j * S + q;
-            const T yo = y[js];
+            const size_t js = (size_t)pp * S + q;
+            const T yo = yv[q];
             const T c = -tg[q];
             const T aa = p.diag ? av[js] : sc.a[q];
             const T dd = p.diag ? dv[js] : sc.d[q];
@@ -428,8 +451,8 @@ cp_forward_kernel(const FwdParams<T> p) {
             const T l = lb[q];
             const T u = ub[q];
             const T yn = clip(yr, l, u);
-            y[js] = yn;
-            ybar[js] = yn + sc.theta[q] * (yn - yo);
+            yv[q] = yn;
+            bv[q] = yn + sc.theta[q] * (yn - yo);
             if (!finite(yn)) fin &= ~(1 << q);
             resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
             ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
@@ -439,6 +462,8 @@ cp_forward_kernel(const FwdParams<T> p) {
             const T inner = (one * yn + c) + t[q];
             stm[q] = pmax(stm[q], fabs(yn - clip(yn - inner, l, u)));
           }
+          store_pack<T, S>(y + (size_t)pp * S, yv);
+          store_pack<T, S>(ybar + (size_t)pp * S, bv);
         }
       }
       publish(1, stm, true);
@@ -448,11 +473,12 @@ cp_forward_kernel(const FwdParams<T> p) {
     __syncthreads();
     // Phase C: constraint residuals of y+.
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      T acc[S];
       const int i = rows.line(sl, lane);
+      const int qp = sl * kC + lane;
       T rbs[S];
 #pragma unroll
-      for (int q = 0; q < S; ++q) rbs[q] = p.rhs[sample(q) * m + (i >= 0 ? i : 0)];
+      for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
+      T acc[S];
       rows.dot(sl, lane, y, acc);
       if (i >= 0) {
 #pragma unroll
@@ -509,13 +535,19 @@ cp_forward_kernel(const FwdParams<T> p) {
     __syncthreads();
   }
 
-  // ---- outputs --------------------------------------------------------------
+  // ---- outputs (back to the external orders) -------------------------------
 #pragma unroll
   for (int q = 0; q < S; ++q) {
     if (!is_valid(q)) continue;
     const int64_t b = sample(q);
-    for (int j = tid; j < n; j += kThreads) p.y_out[b * n + j] = y[(size_t)j * S + q];
-    for (int i = tid; i < m; i += kThreads) p.dual_out[b * m + i] = lam[(size_t)i * S + q];
+    for (int pp = tid; pp < n_pos; pp += kThreads) {
+      const int j = __ldg(sv.c_perm + pp);
+      if (j >= 0) p.y_out[b * n + j] = y[(size_t)pp * S + q];
+    }
+    for (int qp = tid; qp < m_pos; qp += kThreads) {
+      const int i = __ldg(sv.r_perm + qp);
+      if (i >= 0) p.dual_out[b * m + i] = lam[(size_t)qp * S + q];
+    }
     if (tid == 0) {
       p.it_out[b] = sc.count[q];
       p.res_out[b] = sc.res_out[q];
@@ -523,6 +555,20 @@ cp_forward_kernel(const FwdParams<T> p) {
       const bool feas = p.feasible ? (p.feasible[b] != 0) : true;
       p.conv_out[b] = (sc.conv[q] && feas) ? 1 : 0;
     }
+  }
+}
+
+// dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0.
+template <typename T>
+__global__ void permute_rows_kernel(const T* src, int64_t src_stride, const int* perm, int npos,
+                                    int64_t rows, T* dst) {
+  const int64_t total = rows * npos;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = e / npos;
+    const int pp = (int)(e - b * npos);
+    const int k = perm[pp];
+    dst[e] = k >= 0 ? src[b * src_stride + k] : T(0);
   }
 }
 
@@ -584,6 +630,18 @@ cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, 
 }
 
 template <typename T>
+cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int npos, int64_t rows,
+                         T* dst, cudaStream_t stream) {
+  const int64_t total = rows * (int64_t)npos;
+  if (total <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const int blocks = want < 2368 ? (int)want : 2368;
+  permute_rows_kernel<T><<<blocks, threads, 0, stream>>>(src, src_stride, perm, npos, rows, dst);
+  return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
                            cudaStream_t stream) {
   return p.vr ? launch_shared<T, true>(p, S, smem, smem_bytes, stream)
@@ -596,5 +654,9 @@ template size_t forward_static_smem<double>(int);
 template size_t forward_static_smem<float>(int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);
 template cudaError_t arrange_values<float>(const float*, const int*, int, float*, cudaStream_t);
+template cudaError_t permute_rows<double>(const double*, int64_t, const int*, int, int64_t, double*,
+                                          cudaStream_t);
+template cudaError_t permute_rows<float>(const float*, int64_t, const int*, int, int64_t, float*,
+                                         cudaStream_t);
 
 }  // namespace purin

@@ -41,9 +41,16 @@ struct FwdParams {
   int diag;
   int partitionable;
   T* gstate;  // per-tile state in global memory when it does not fit in shared memory
-  SellView sell;  // sliced-ELL rows/columns for C = 32 / S
+  SellView sell;  // sliced-ELL rows/columns in the internal orders
   const T* vr;    // shared values in SELL row order (null: per-sample values via slots)
   const T* vc;    // shared values in SELL column order
+  // Per-sample inputs permuted into the internal orders (zero at padding positions).
+  const T* tgt_i;    // (B, n_pos)
+  const T* rhs_i;    // (B, m_pos)
+  const T* dual0_i;  // (B, m_pos) or null
+  const T* lo_i;     // (B or 1, n_pos)
+  const T* up_i;
+  int64_t bstride_i;  // 0 (shared bounds) or n_pos
 };
 
 template <typename T>
@@ -133,6 +140,10 @@ template <typename T>
 size_t forward_static_smem(int S);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
+// dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0 for b < rows.
+template <typename T>
+cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int npos, int64_t rows,
+                         T* dst, cudaStream_t stream);
 
 // Adjoint: shared-memory bytes for one CTA, occupancy-limited cooperative grid.
 template <typename T>

@@ -59,7 +59,7 @@ struct PurinCpPlan {
   std::vector<int32_t> kept_row_ptr, kept_cols;
   int sm_count = 0;
   int max_smem_optin = 0;
-  // Sliced-ELL layouts for C = 32, 16, 8, 4, 2, 1 (index log2(32 / C)), built at creation.
-  purin::SellView sell[6];
+  // Sliced-ELL layout (C = 32) in the internal row/column orders, built at creation.
+  purin::SellView sell[1];
   void* sell_block = nullptr;
 };

@@ -1,16 +1,21 @@
-// Sliced-ELL (SELL-C-sigma) views of the kept-row operator K and of K.T.
+// Sliced-ELL (SELL-32-sigma) views of the kept-row operator K and of K.T, in the
+// kernels' internal row and column orders.
 //
 // Rows (for K @ x) and columns (for K.T @ y) are sorted by their number of
-// nonzeros (descending, stable) and grouped in slices of C consecutive sorted
-// rows; slice s stores its entries slot-major at ptr[s] + k * C + lane for
-// k < width(s).  A warp whose C lane-groups each own one row of the slice
-// therefore reads C consecutive entries per step (coalesced), and the slice
-// width bounds the per-row loop.  Entries past a row's length are padding:
-// index = the padded element of the gathered vector (always zero) and
-// value 0, so they add exact zeros after the row's real terms.  Within a row
-// entries keep their original order (CSR order for rows; ascending row, i.e.
-// the reference scatter's update order, for columns), so sums round exactly
-// as the reference's sequential accumulation.
+// nonzeros (descending, stable) and grouped in slices of 32 consecutive sorted
+// lines; slice s stores its entries slot-major at ptr[s] + k * 32 + lane for
+// k < width(s), so a warp whose lanes each own one line of the slice reads 32
+// consecutive entries per step.  The sorted order is also the kernels' internal
+// order: internal column position p holds external variable c_perm[p], internal
+// row position q holds kept row r_perm[q] (-1 marks the padding positions that
+// complete the last slice), and the entries' indices are internal positions.
+// Per-sample vectors are permuted into these orders once per call so every
+// per-iteration access is coalesced.  Entries past a line's length are
+// padding: index = the extra zero element at position n_pos (or m_pos) of the
+// gathered vector, value 0, so they add exact zeros after the line's real
+// terms.  Within a line entries keep their original order (CSR order for rows;
+// ascending row, i.e. the reference scatter's update order, for columns), so
+// sums round exactly as the reference's sequential accumulation.
 #pragma once
 
 #include <stdint.h>
@@ -18,16 +23,17 @@
 namespace purin {
 
 struct SellView {
-  int C;
+  int C;                 // slice height (32)
   int nsl_r, nsl_c;      // slices
   int nnz_r, nnz_c;      // stored entries (with padding)
+  int m_pos, n_pos;      // internal row / column positions (nsl * 32)
   const int* r_ptr;      // nsl_r + 1 entry offsets
-  const int* r_perm;     // nsl_r * C: kept row of each sorted position, -1 for padding rows
-  const int* r_idx;      // nnz_r: column index, n for padding
+  const int* r_perm;     // m_pos: kept row of each internal row position, -1 for padding
+  const int* r_idx;      // nnz_r: internal column position, n_pos for padding
   const int* r_slot;     // nnz_r: kept CSR slot, -1 for padding
   const int* c_ptr;      // nsl_c + 1
-  const int* c_perm;     // nsl_c * C: column of each sorted position, -1 for padding
-  const int* c_idx;      // nnz_c: kept row index, m for padding
+  const int* c_perm;     // n_pos: variable of each internal column position, -1 for padding
+  const int* c_idx;      // nnz_c: internal row position, m_pos for padding
   const int* c_slot;     // nnz_c: kept CSR slot, -1 for padding
 };
 

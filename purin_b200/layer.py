@@ -174,6 +174,11 @@ class PreparedChambollePockProjection:
         set_("_bound_slots", as_long(plan.indices(_native.BOUND_SLOTS)))
         set_("_bound_vars", as_long(plan.indices(_native.BOUND_VARIABLES)))
         set_("_n_bound", int(plan.info.bound_rows))
+        param_rows = getattr(self.canonical, "rhs_parameter_rows", None)
+        bound_rows = plan.indices(_native.BOUND_ROWS)
+        set_("_bounds_shared", bool(
+            getattr(self.canonical, "values_constant", False) and param_rows is not None
+            and not np.asarray(param_rows, bool)[bound_rows].any()))
         set_("_kept_ell", as_long(ell_index(kept_row_ptr)))
         set_("_slot_row", as_long(rows_of(kept_row_ptr)))
         cfg = self.config
@@ -304,14 +309,17 @@ class PreparedChambollePockProjection:
         """Box bounds from singleton inequality rows (bounds.py:193-209)."""
         n, dev, dt = self.output_size, self._device, self._tdtype
         inf = torch.tensor(float("inf"), dtype=dt, device=dev)
-        rows_b = 1 if (values.shape[0] == 1 and rhs.shape[0] == 1) else batch
+        # Bounds are computed once for the whole batch when neither the bound rows'
+        # coefficients nor their right-hand sides depend on the parameters.
+        shared = values.shape[0] == 1 and (rhs.shape[0] == 1 or self._bounds_shared)
+        rows_b = 1 if shared else batch
         lower = torch.full((rows_b, n), -float("inf"), dtype=dt, device=dev)
         upper = torch.full((rows_b, n), float("inf"), dtype=dt, device=dev)
         if self._n_bound == 0:
             feasible = torch.ones((batch,), dtype=torch.uint8, device=dev)
             return lower, upper, feasible, None, None
         coefficient = values[:, self._bound_slots].expand(rows_b, -1)
-        b_rhs = rhs[:, self._bound_rows].expand(rows_b, -1)
+        b_rhs = rhs[:rows_b, self._bound_rows].expand(rows_b, -1)
         threshold = b_rhs / torch.where(coefficient != 0, coefficient, torch.ones_like(coefficient))
         index = self._bound_vars.unsqueeze(0).expand(rows_b, -1)
         lower = lower.scatter_reduce(1, index, torch.where(coefficient < 0, threshold, -inf), "amax",
