@@ -18,7 +18,11 @@
 //                                                                     kernels.py:138-150,153-175,272-274
 //   C (rows)    K y+ - rhs for the equality/inequality residuals      kernels.py:155-157
 // followed by a per-sample reduction and the accept/freeze decision
-// (kernels.py:262-283).  A frozen sample never changes again, so the tile
+// (kernels.py:262-283).  Pass C only feeds the acceptance test and the
+// residual reported for the final iterate, so it runs when some active sample
+// of the tile passes every other test (gap, stationarity, bound violation,
+// finiteness) and on the last iteration; otherwise no sample can be accepted
+// whatever its value, and every output is the same.  A frozen sample never changes again, so the tile
 // exits as soon as all its samples are accepted; iterations and results are
 // those of the reference's batch-wide loop.
 #include <cuda_runtime.h>
@@ -39,7 +43,9 @@ struct TileScratch {
   T tau[S], sigma[S], theta[S], a[S], d[S], tol[S];
   T res_out[S], gap_out[S];
   int active[S], count[S], conv[S];
-  T red[kWarps][S][5];
+  T gap_it[S], stat_it[S], resb_it[S];
+  int fin_it[S], need_c[S];
+  T red[kWarps][S][6];
   int redf[kWarps][S];
   T s_red[kWarps][S];
 };
@@ -367,8 +373,9 @@ cp_forward_kernel(const FwdParams<T> p) {
   }
   __syncthreads();
 
-  // Warp partials of the per-sample diagnostics: [warp][sample][0..4] =
-  // residual max, stationarity max, primal sum, dual sum, rhs.dual sum.
+  // Warp partials of the per-sample diagnostics: [warp][sample][0..5] = bound
+  // violation max, stationarity max, primal sum, dual sum, rhs.dual sum,
+  // constraint residual max.
   auto publish = [&](int slot, T (&v)[S], bool is_max) {
 #pragma unroll
     for (int q = 0; q < S; ++q) {
@@ -466,43 +473,28 @@ cp_forward_kernel(const FwdParams<T> p) {
           store_pack<T, S>(ybar + (size_t)pp * S, bv);
         }
       }
+      publish(0, resm, true);  // bound violation part of the residual
       publish(1, stm, true);
       publish(2, ps, false);
       publish(3, ds, false);
     }
-    __syncthreads();
-    // Phase C: constraint residuals of y+.
-    for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
-      const int i = rows.line(sl, lane);
-      const int qp = sl * kC + lane;
-      T rbs[S];
-#pragma unroll
-      for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
-      T acc[S];
-      rows.dot(sl, lane, y, acc);
-      if (i >= 0) {
-#pragma unroll
-        for (int q = 0; q < S; ++q) {
-          if (!((act >> q) & 1)) continue;
-          const T r = acc[q] - rbs[q];
-          resm[q] = pmax(resm[q], i < me ? fabs(r) : pmax(r, zero));
-        }
-      }
-    }
-    publish(0, resm, true);
     fin = __reduce_and_sync(kFullMask, (unsigned)fin);
     if (lane == 0) {
 #pragma unroll
       for (int q = 0; q < S; ++q) sc.redf[warp][q] = (fin >> q) & 1;
     }
     __syncthreads();
+    // Gap, stationarity, bound violation and finiteness are known now.  The
+    // feasibility residual of y+ (phase C) can only change an outcome if some
+    // active sample passes every other test, and it is reported for the last
+    // iteration; otherwise this iteration rejects every sample without it.
     if (tid < S) {
       const int q = tid;
-      T res = zero, stat = zero, P = zero, Dp = zero, Rd = zero;
+      T resb = zero, stat = zero, P = zero, Dp = zero, Rd = zero;
       int f = 1;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        res = pmax(res, sc.red[w][q][0]);
+        resb = pmax(resb, sc.red[w][q][0]);
         stat = pmax(stat, sc.red[w][q][1]);
         P = P + sc.red[w][q][2];
         Dp = Dp + sc.red[w][q][3];
@@ -511,9 +503,53 @@ cp_forward_kernel(const FwdParams<T> p) {
       }
       const T D = Dp - Rd;
       const T gap = pmax(P - D, zero) / pmax(one, pmax(fabs(P), fabs(D)));
-      const bool finite_all = f && finite(gap);
       const T tol = sc.tol[q];
-      const bool accepted = finite_all && res <= tol && gap <= tol && stat <= tol;
+      const bool finite_all = f && finite(gap);
+      sc.gap_it[q] = gap;
+      sc.stat_it[q] = stat;
+      sc.resb_it[q] = resb;
+      sc.fin_it[q] = finite_all ? 1 : 0;
+      sc.need_c[q] = (sc.active[q] && finite_all && resb <= tol && gap <= tol && stat <= tol) ? 1 : 0;
+    }
+    __syncthreads();
+    bool need_c = it + 1 == p.max_iterations;
+#pragma unroll
+    for (int q = 0; q < S; ++q) need_c |= sc.need_c[q] != 0;
+    if (need_c) {
+      // Phase C: constraint residuals of y+.
+      T resc[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) resc[q] = zero;
+      for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
+        const int i = rows.line(sl, lane);
+        const int qp = sl * kC + lane;
+        T rbs[S];
+#pragma unroll
+        for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
+        T acc[S];
+        rows.dot(sl, lane, y, acc);
+        if (i >= 0) {
+#pragma unroll
+          for (int q = 0; q < S; ++q) {
+            if (!((act >> q) & 1)) continue;
+            const T r = acc[q] - rbs[q];
+            resc[q] = pmax(resc[q], i < me ? fabs(r) : pmax(r, zero));
+          }
+        }
+      }
+      publish(5, resc, true);
+      __syncthreads();
+    }
+    if (tid < S) {
+      const int q = tid;
+      T res = sc.resb_it[q];
+      if (need_c) {
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) res = pmax(res, sc.red[w][q][5]);
+      }
+      const T gap = sc.gap_it[q], stat = sc.stat_it[q];
+      const T tol = sc.tol[q];
+      const bool accepted = need_c && sc.fin_it[q] && res <= tol && gap <= tol && stat <= tol;
       if (sc.active[q]) {
         sc.count[q] += 1;
         sc.res_out[q] = pmax(res, stat);
