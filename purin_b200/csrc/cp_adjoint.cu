@@ -178,11 +178,15 @@ __device__ void basis_dots(const T* V, int W, const T* buf, int r, T* out, T* re
     T part[kChunk];
 #pragma unroll
     for (int q = 0; q < kChunk; ++q) part[q] = T(0);
+#pragma unroll 2
     for (int e = threadIdx.x; e < W; e += kThreads) {
       const T be = buf[e];
+      T v[kChunk];
+#pragma unroll
+      for (int q = 0; q < kChunk; ++q) v[q] = (c0 + q < r) ? V[(size_t)(c0 + q) * W + e] : T(0);
 #pragma unroll
       for (int q = 0; q < kChunk; ++q)
-        if (c0 + q < r) part[q] = part[q] + V[(size_t)(c0 + q) * W + e] * be;
+        if (c0 + q < r) part[q] = part[q] + v[q] * be;
     }
 #pragma unroll
     for (int q = 0; q < kChunk; ++q) part[q] = warp_sum(part[q]);
@@ -201,14 +205,27 @@ __device__ void basis_dots(const T* V, int W, const T* buf, int r, T* out, T* re
   }
 }
 
+// sum_i c[i] V[i][e] over rows [0, r), accumulated in row order; the basis
+// values are loaded kChunk at a time so the loads are independent.
+template <typename T>
+__device__ __forceinline__ T basis_combination(const T* V, int W, int e, int r, const T* c) {
+  T acc = T(0);
+  for (int c0 = 0; c0 < r; c0 += kChunk) {
+    T v[kChunk];
+#pragma unroll
+    for (int q = 0; q < kChunk; ++q) v[q] = (c0 + q < r) ? V[(size_t)(c0 + q) * W + e] : T(0);
+#pragma unroll
+    for (int q = 0; q < kChunk; ++q)
+      if (c0 + q < r) acc = acc + c[c0 + q] * v[q];
+  }
+  return acc;
+}
+
 // buf <- buf - sum_i c[i] V[i] over rows [0, r) (CGS pass, second half).
 template <typename T>
 __device__ void basis_update(const T* V, int W, T* buf, int r, const T* c) {
-  for (int e = threadIdx.x; e < W; e += kThreads) {
-    T acc = T(0);
-    for (int i = 0; i < r; ++i) acc = acc + c[i] * V[(size_t)i * W + e];
-    buf[e] = buf[e] - acc;
-  }
+#pragma unroll 2
+  for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = buf[e] - basis_combination(V, W, e, r, c);
   __syncthreads();
 }
 
@@ -479,12 +496,9 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         }
       }
       __syncthreads();
+#pragma unroll 2
       for (int e = threadIdx.x; e < W; e += kThreads) {
-        T corr = zero;
-        for (int q = 0; q < R; ++q) {
-          if (q < row_steps) corr = corr + bsv[q] * V[(size_t)q * W + e];
-        }
-        const T cand = x[e] + corr;
+        const T cand = x[e] + basis_combination(V, W, e, row_steps, bsv);
         buf[e] = cand;
         x[e] = cand;
       }
