@@ -62,10 +62,14 @@ struct FwdPlan {
   int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
 
-FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch);
+FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
+                           bool shared_values);
 
-FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
-  FwdPlan fp = plan_forward_tiles(plan, cfg, batch);
+// The workspace does not depend on shared_values: it only ranks tile widths
+// whose state fits in shared memory, which need no workspace for the state.
+FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
+                     bool shared_values = true) {
+  FwdPlan fp = plan_forward_tiles(const_cast<PurinCpPlan*>(plan), cfg, batch, shared_values);
   const size_t w = dtype_size(plan->info.dtype);
   fp.sell_index = 0;  // one lane per line: slices of C = 32 for every tile width
   const purin::SellView& sv = plan->sell[fp.sell_index];
@@ -84,34 +88,46 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   return fp;
 }
 
-FwdPlan plan_forward_tiles(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch) {
+FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
+                           bool shared_values) {
   FwdPlan fp;
-  const int n = plan->info.n, m = plan->info.kept_rows;
   const size_t w = dtype_size(plan->info.dtype);
+  const bool f64 = plan->info.dtype == PURIN_FLOAT64;
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
-  (void)n;
-  (void)m;
   const int n_pos = plan->sell[0].n_pos, m_pos = plan->sell[0].m_pos;
   const size_t per_sample =
       (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
-  const int64_t target_tiles = 2 * (int64_t)std::max(1, plan->sm_count);
+  const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it fits.
   int forced = 0;
   if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
+  // Default: the tile width whose resident CTAs hold the most warps over the
+  // batch (the iteration is latency-bound), then the most samples, then the
+  // narrowest.  Every width whose state fits in shared memory is a candidate.
   int best = 0;
-  for (int S = 1; S <= 8; S *= 2) {
-    const size_t stat = plan->info.dtype == PURIN_FLOAT64 ? purin::forward_static_smem<double>(S)
-                                                          : purin::forward_static_smem<float>(S);
+  int64_t best_warps = -1, best_samples = -1;
+  for (int S = 1, k = 0; S <= 8; S *= 2, ++k) {
+    const size_t stat = f64 ? purin::forward_static_smem<double>(S) : purin::forward_static_smem<float>(S);
     if ((size_t)S * per_sample + stat + 1024 > cap) break;
-    const int64_t tiles = (batch + S - 1) / S;
-    // Default: the widest tile that still leaves room for two CTAs per SM and
-    // gives every SM at least two tiles.
-    const bool two_per_sm = 2 * ((size_t)S * per_sample + stat + 1024) <= cap;
     if (forced > 0) {
       if (S <= forced) best = S;
-    } else if (S == 1 || (tiles >= target_tiles && two_per_sm)) {
+      continue;
+    }
+    int& cached = plan->fwd_blocks[diag ? 1 : 0][shared_values ? 1 : 0][k];
+    if (cached < 0) {
+      const size_t dyn = (size_t)S * per_sample;
+      cached = f64 ? purin::forward_blocks_per_sm<double>(S, shared_values, dyn)
+                   : purin::forward_blocks_per_sm<float>(S, shared_values, dyn);
+    }
+    const int64_t tiles = (batch + S - 1) / S;
+    const int64_t ctas = std::min<int64_t>(tiles, sms * std::max(cached, 0));
+    const int64_t warps = ctas * (purin::kForwardThreads / 32);
+    const int64_t samples = std::min<int64_t>(batch, ctas * S);
+    if (best == 0 || warps > best_warps || (warps == best_warps && samples > best_samples)) {
       best = S;
+      best_warps = warps;
+      best_samples = samples;
     }
   }
   if (best > 0) {
@@ -200,13 +216,13 @@ int32_t check_linear(const PurinLinearSolverConfig* lin) {
 template <typename T>
 int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinCpForwardArgs* a,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const FwdPlan fp = plan_forward(plan, cfg, a->batch);
+  const bool shared = a->values_stride == 0 || a->batch == 1;
+  const FwdPlan fp = plan_forward(plan, cfg, a->batch, shared);
   if (workspace == nullptr || workspace_bytes < fp.workspace)
     return fail(PURIN_ERR_WORKSPACE, "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes");
   char* ws = static_cast<char*>(workspace);
   const purin::SellView& sv = plan->sell[fp.sell_index];
   // Values shared by the batch are arranged once per call in both sliced-ELL orders.
-  const bool shared = a->values_stride == 0 || a->batch == 1;
   T* vr = nullptr;
   T* vc = nullptr;
   if (shared && plan->info.kept_nnz > 0) {

@@ -11,21 +11,27 @@
 // layout with C = 32: a warp owns a slice of 32 rows (or columns), each lane
 // one line, and each lane carries that line for all S samples of the tile, so
 // one index load and one value load feed S multiply-adds whose operands arrive
-// as one vector shared-memory load.  Each iteration makes three passes:
-//   A (rows)    lambda+ = proj(lambda + sigma (K ybar - rhs))         kernels.py:133-137
-//   B (columns) t = K.T lambda+, y+ = clip(a y - d t + o), ybar+,
-//               bound violation, primal/dual objective terms, stationarity
-//                                                                     kernels.py:138-150,153-175,272-274
-//   C (rows)    K y+ - rhs for the equality/inequality residuals      kernels.py:155-157
+// as one vector shared-memory load.  An iteration makes these passes:
+//   A  (rows)    lambda+ = proj(lambda + sigma (K ybar - rhs))         kernels.py:133-137
+//   B  (columns) t = K.T lambda+, y+ = clip(a y - d t + o), ybar+,
+//                stationarity                                         kernels.py:138-150,272-274
+//   B2 (rows, columns) rhs . lambda+, bound violation and the primal/dual
+//                objectives of y+ (t = K.T lambda+ again)             kernels.py:153-175
+//   C  (rows)    K y+ - rhs for the equality/inequality residuals      kernels.py:155-157
 // followed by a per-sample reduction and the accept/freeze decision
-// (kernels.py:262-283).  Pass C only feeds the acceptance test and the
-// residual reported for the final iterate, so it runs when some active sample
-// of the tile passes every other test (gap, stationarity, bound violation,
-// finiteness) and on the last iteration; otherwise no sample can be accepted
-// whatever its value, and every output is the same.  A frozen sample never changes again, so the tile
+// (kernels.py:262-283).  B2 and C only feed the acceptance test and the values
+// reported for the final iterate.  B2 runs when some active sample of the tile
+// has finite iterates and stationarity within tolerance, C when one also passes
+// the gap and bound tests, and both on the last iteration; otherwise no sample
+// can be accepted whatever their values, and every output is the same.  After
+// the first iteration that needs B2, passes A and B accumulate its sums
+// themselves (same lanes, same order), since a converging tile needs them on
+// most later iterations.  A frozen sample never changes again, so the tile
 // exits as soon as all its samples are accepted; iterations and results are
 // those of the reference's batch-wide loop.
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "cp_kernels.cuh"
@@ -34,7 +40,7 @@ namespace purin {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = kForwardThreads;
 constexpr int kWarps = kThreads / 32;
 constexpr int kC = 32;  // sliced-ELL slice height: one row per lane
 
@@ -189,7 +195,7 @@ __device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
 }
 
 template <typename T, int S, bool kSmem, bool kShared>
-__global__ void __launch_bounds__(kThreads, (S <= 2) ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, (S == 1) ? 4 : (S <= 2) ? 2 : 1)
 cp_forward_kernel(const FwdParams<T> p) {
   extern __shared__ __align__(16) unsigned char dyn_smem[];
   __shared__ TileScratch<T, S> sc;
@@ -383,51 +389,169 @@ cp_forward_kernel(const FwdParams<T> p) {
       if (lane == 0) sc.red[warp][q][slot] = r;
     }
   };
+  // Phase A: dual update; with kFull also the dual objective term rhs . lambda+.
+  auto phase_a = [&](auto full_c, int act, int& fin) {
+    constexpr bool kFull = decltype(full_c)::value;
+    T rd[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) rd[q] = zero;
+    for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
+      const int i = rows.line(sl, lane);
+      const int qp = sl * kC + lane;
+      // Per-sample operands are loaded before the product so their latency overlaps it.
+      T rbs[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
+      T acc[S];
+      rows.dot(sl, lane, ybar, acc);
+      if (i >= 0) {
+        T lv[S];
+        load_pack<T, S>(lam + (size_t)qp * S, lv);
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          if (!((act >> q) & 1)) continue;
+          const T sg = p.diag ? sv_[(size_t)qp * S + q] : sc.sigma[q];
+          const T raw = lv[q] + sg * (acc[q] - rbs[q]);
+          const T nl = i < me ? raw : pmax(raw, zero);
+          lv[q] = nl;
+          if (!finite(nl)) fin &= ~(1 << q);
+          if constexpr (kFull) rd[q] = rd[q] + rbs[q] * nl;
+        }
+        store_pack<T, S>(lam + (size_t)qp * S, lv);
+      }
+    }
+    if constexpr (kFull) publish(4, rd, false);
+  };
+  // Phase B: primal update and stationarity; with kFull also the bound
+  // violation and the primal and dual objectives of y+.
+  auto phase_b = [&](auto full_c, int act, int& fin) {
+    constexpr bool kFull = decltype(full_c)::value;
+    T stm[S], resm[S], ps[S], ds[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) stm[q] = resm[q] = ps[q] = ds[q] = zero;
+    for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
+      const int j = cols.line(sl, lane);
+      const int pp = sl * kC + lane;
+      T tg[S], lb[S], ub[S];
+#pragma unroll
+      for (int q = 0; q < S; ++q) {
+        const int64_t b = sample(q);
+        tg[q] = p.tgt_i[b * n_pos + pp];
+        lb[q] = p.lo_i[b * p.bstride_i + pp];
+        ub[q] = p.up_i[b * p.bstride_i + pp];
+      }
+      T t[S];
+      cols.dot(sl, lane, lam, t);
+      if (j >= 0) {
+        T yv[S], bv[S];
+        load_pack<T, S>(y + (size_t)pp * S, yv);
+        load_pack<T, S>(ybar + (size_t)pp * S, bv);
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          if (!((act >> q) & 1)) continue;
+          const size_t js = (size_t)pp * S + q;
+          const T yo = yv[q];
+          const T c = -tg[q];
+          const T aa = p.diag ? av[js] : sc.a[q];
+          const T dd = p.diag ? dv[js] : sc.d[q];
+          const T off = (-dd) * c;
+          const T yr = (aa * yo - dd * t[q]) + off;
+          const T l = lb[q];
+          const T u = ub[q];
+          const T yn = clip(yr, l, u);
+          yv[q] = yn;
+          bv[q] = yn + sc.theta[q] * (yn - yo);
+          if (!finite(yn)) fin &= ~(1 << q);
+          if constexpr (kFull) {
+            resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
+            ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
+            const T tt = c + t[q];
+            const T mn = clip(-tt / one, l, u);
+            ds[q] = ds[q] + (T(0.5) * one * (mn * mn) + tt * mn);
+          }
+          const T inner = (one * yn + c) + t[q];
+          stm[q] = pmax(stm[q], fabs(yn - clip(yn - inner, l, u)));
+        }
+        store_pack<T, S>(y + (size_t)pp * S, yv);
+        store_pack<T, S>(ybar + (size_t)pp * S, bv);
+      }
+    }
+    publish(1, stm, true);
+    if constexpr (kFull) {
+      publish(0, resm, true);  // bound violation part of the residual
+      publish(2, ps, false);
+      publish(3, ds, false);
+    }
+  };
+  // Once a tile has needed the full stopping test it keeps evaluating it inside
+  // phases A and B (a converging tile needs it on most later iterations); before
+  // that, phase B2 recomputes the same sums in the same order when required.
+  bool full = false;
   for (int it = 0; it < p.max_iterations; ++it) {
     int act = 0;
 #pragma unroll
     for (int q = 0; q < S; ++q) act |= (sc.active[q] != 0) << q;
     if (!act) break;
+    const bool last = it + 1 == p.max_iterations;
     int fin = (1 << S) - 1;
-    {
-      // Phase A: dual update.
+    if (full) phase_a(std::true_type{}, act, fin);
+    else phase_a(std::false_type{}, act, fin);
+    __syncthreads();
+    if (full) phase_b(std::true_type{}, act, fin);
+    else phase_b(std::false_type{}, act, fin);
+    fin = __reduce_and_sync(kFullMask, (unsigned)fin);
+    if (lane == 0) {
+#pragma unroll
+      for (int q = 0; q < S; ++q) sc.redf[warp][q] = (fin >> q) & 1;
+    }
+    __syncthreads();
+    // Acceptance needs finite iterates and stationarity within tolerance.  The
+    // gap and bound violation (phases A/B with `full`, else phase B2) are used
+    // only when some active sample passes those tests, the feasibility residual
+    // of y+ (phase C) only when some sample also passes the gap and bound tests,
+    // and both on the last iteration, whose values are reported.  An iteration
+    // that skips them rejects every sample, as the full test would.
+    if (tid < S) {
+      const int q = tid;
+      T stat = zero;
+      int f = 1;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        stat = pmax(stat, sc.red[w][q][1]);
+        f &= sc.redf[w][q];
+      }
+      sc.stat_it[q] = stat;
+      sc.fin_it[q] = f;
+      sc.need_c[q] = (sc.active[q] && f && stat <= sc.tol[q]) ? 1 : 0;
+    }
+    __syncthreads();
+    bool need_gap = last;
+#pragma unroll
+    for (int q = 0; q < S; ++q) need_gap |= sc.need_c[q] != 0;
+    bool need_c = last;
+    if (need_gap && !full) {
+      // Phase B2: dual objective term rhs . lambda+ (rows), primal and dual
+      // objectives of y+ and the bound violation (columns, t = K^T lambda+ again).
       T rd[S];
 #pragma unroll
       for (int q = 0; q < S; ++q) rd[q] = zero;
       for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
         const int i = rows.line(sl, lane);
         const int qp = sl * kC + lane;
-        // Per-sample operands are loaded before the product so their latency overlaps it.
-        T rbs[S];
-#pragma unroll
-        for (int q = 0; q < S; ++q) rbs[q] = p.rhs_i[sample(q) * m_pos + qp];
-        T acc[S];
-        rows.dot(sl, lane, ybar, acc);
         if (i >= 0) {
           T lv[S];
           load_pack<T, S>(lam + (size_t)qp * S, lv);
 #pragma unroll
           for (int q = 0; q < S; ++q) {
             if (!((act >> q) & 1)) continue;
-            const T sg = p.diag ? sv_[(size_t)qp * S + q] : sc.sigma[q];
-            const T raw = lv[q] + sg * (acc[q] - rbs[q]);
-            const T nl = i < me ? raw : pmax(raw, zero);
-            lv[q] = nl;
-            if (!finite(nl)) fin &= ~(1 << q);
-            rd[q] = rd[q] + rbs[q] * nl;
+            rd[q] = rd[q] + p.rhs_i[sample(q) * m_pos + qp] * lv[q];
           }
-          store_pack<T, S>(lam + (size_t)qp * S, lv);
         }
       }
       publish(4, rd, false);
-    }
-    __syncthreads();
-    T resm[S];
-    {
-      // Phase B: primal update and column diagnostics.
-      T stm[S], ps[S], ds[S];
+      T resm[S], ps[S], ds[S];
 #pragma unroll
-      for (int q = 0; q < S; ++q) resm[q] = stm[q] = ps[q] = ds[q] = zero;
+      for (int q = 0; q < S; ++q) resm[q] = ps[q] = ds[q] = zero;
       for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
         const int j = cols.line(sl, lane);
         const int pp = sl * kC + lane;
@@ -442,79 +566,54 @@ cp_forward_kernel(const FwdParams<T> p) {
         T t[S];
         cols.dot(sl, lane, lam, t);
         if (j >= 0) {
-          T yv[S], bv[S];
+          T yv[S];
           load_pack<T, S>(y + (size_t)pp * S, yv);
-          load_pack<T, S>(ybar + (size_t)pp * S, bv);
 #pragma unroll
           for (int q = 0; q < S; ++q) {
             if (!((act >> q) & 1)) continue;
-            const size_t js = (size_t)pp * S + q;
-            const T yo = yv[q];
+            const T yn = yv[q];
             const T c = -tg[q];
-            const T aa = p.diag ? av[js] : sc.a[q];
-            const T dd = p.diag ? dv[js] : sc.d[q];
-            const T off = (-dd) * c;
-            const T yr = (aa * yo - dd * t[q]) + off;
             const T l = lb[q];
             const T u = ub[q];
-            const T yn = clip(yr, l, u);
-            yv[q] = yn;
-            bv[q] = yn + sc.theta[q] * (yn - yo);
-            if (!finite(yn)) fin &= ~(1 << q);
             resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
             ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
             const T tt = c + t[q];
             const T mn = clip(-tt / one, l, u);
             ds[q] = ds[q] + (T(0.5) * one * (mn * mn) + tt * mn);
-            const T inner = (one * yn + c) + t[q];
-            stm[q] = pmax(stm[q], fabs(yn - clip(yn - inner, l, u)));
           }
-          store_pack<T, S>(y + (size_t)pp * S, yv);
-          store_pack<T, S>(ybar + (size_t)pp * S, bv);
         }
       }
       publish(0, resm, true);  // bound violation part of the residual
-      publish(1, stm, true);
       publish(2, ps, false);
       publish(3, ds, false);
     }
-    fin = __reduce_and_sync(kFullMask, (unsigned)fin);
-    if (lane == 0) {
+    if (need_gap) {
+      __syncthreads();
+      if (tid < S) {
+        const int q = tid;
+        T resb = zero, P = zero, Dp = zero, Rd = zero;
 #pragma unroll
-      for (int q = 0; q < S; ++q) sc.redf[warp][q] = (fin >> q) & 1;
-    }
-    __syncthreads();
-    // Gap, stationarity, bound violation and finiteness are known now.  The
-    // feasibility residual of y+ (phase C) can only change an outcome if some
-    // active sample passes every other test, and it is reported for the last
-    // iteration; otherwise this iteration rejects every sample without it.
-    if (tid < S) {
-      const int q = tid;
-      T resb = zero, stat = zero, P = zero, Dp = zero, Rd = zero;
-      int f = 1;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        resb = pmax(resb, sc.red[w][q][0]);
-        stat = pmax(stat, sc.red[w][q][1]);
-        P = P + sc.red[w][q][2];
-        Dp = Dp + sc.red[w][q][3];
-        Rd = Rd + sc.red[w][q][4];
-        f &= sc.redf[w][q];
+        for (int w = 0; w < kWarps; ++w) {
+          resb = pmax(resb, sc.red[w][q][0]);
+          P = P + sc.red[w][q][2];
+          Dp = Dp + sc.red[w][q][3];
+          Rd = Rd + sc.red[w][q][4];
+        }
+        const T D = Dp - Rd;
+        const T gap = pmax(P - D, zero) / pmax(one, pmax(fabs(P), fabs(D)));
+        const T tol = sc.tol[q];
+        const bool finite_all = sc.fin_it[q] && finite(gap);
+        sc.gap_it[q] = gap;
+        sc.resb_it[q] = resb;
+        sc.fin_it[q] = finite_all ? 1 : 0;
+        sc.need_c[q] =
+            (sc.active[q] && finite_all && resb <= tol && gap <= tol && sc.stat_it[q] <= tol) ? 1 : 0;
       }
-      const T D = Dp - Rd;
-      const T gap = pmax(P - D, zero) / pmax(one, pmax(fabs(P), fabs(D)));
-      const T tol = sc.tol[q];
-      const bool finite_all = f && finite(gap);
-      sc.gap_it[q] = gap;
-      sc.stat_it[q] = stat;
-      sc.resb_it[q] = resb;
-      sc.fin_it[q] = finite_all ? 1 : 0;
-      sc.need_c[q] = (sc.active[q] && finite_all && resb <= tol && gap <= tol && stat <= tol) ? 1 : 0;
-    }
-    __syncthreads();
-    bool need_c = it + 1 == p.max_iterations;
+      __syncthreads();
 #pragma unroll
-    for (int q = 0; q < S; ++q) need_c |= sc.need_c[q] != 0;
+      for (int q = 0; q < S; ++q) need_c |= sc.need_c[q] != 0;
+      full = true;
+    }
     if (need_c) {
       // Phase C: constraint residuals of y+.
       T resc[S];
@@ -542,18 +641,21 @@ cp_forward_kernel(const FwdParams<T> p) {
     }
     if (tid < S) {
       const int q = tid;
-      T res = sc.resb_it[q];
-      if (need_c) {
+      bool accepted = false;
+      if (need_c) {  // need_c implies that phase B2 ran
+        T res = sc.resb_it[q];
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) res = pmax(res, sc.red[w][q][5]);
+        const T gap = sc.gap_it[q], stat = sc.stat_it[q];
+        const T tol = sc.tol[q];
+        accepted = sc.fin_it[q] && res <= tol && gap <= tol && stat <= tol;
+        if (sc.active[q]) {
+          sc.res_out[q] = pmax(res, stat);
+          sc.gap_out[q] = gap;
+        }
       }
-      const T gap = sc.gap_it[q], stat = sc.stat_it[q];
-      const T tol = sc.tol[q];
-      const bool accepted = need_c && sc.fin_it[q] && res <= tol && gap <= tol && stat <= tol;
       if (sc.active[q]) {
         sc.count[q] += 1;
-        sc.res_out[q] = pmax(res, stat);
-        sc.gap_out[q] = gap;
         sc.conv[q] = accepted ? 1 : 0;
         if (accepted) sc.active[q] = 0;
       }
@@ -644,7 +746,36 @@ cudaError_t launch_shared(const FwdParams<T>& p, int S, bool smem, size_t smem_b
   }
 }
 
+template <typename T, int S, bool kShared>
+int blocks_per_sm_s(size_t smem_bytes) {
+  auto kern = cp_forward_kernel<T, S, true, kShared>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes) !=
+      cudaSuccess)
+    return 0;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem_bytes) != cudaSuccess)
+    return 0;
+  return per_sm;
+}
+
+template <typename T, bool kShared>
+int blocks_per_sm_shared(int S, size_t smem_bytes) {
+  switch (S) {
+    case 1: return blocks_per_sm_s<T, 1, kShared>(smem_bytes);
+    case 2: return blocks_per_sm_s<T, 2, kShared>(smem_bytes);
+    case 4: return blocks_per_sm_s<T, 4, kShared>(smem_bytes);
+    case 8: return blocks_per_sm_s<T, 8, kShared>(smem_bytes);
+    default: return 0;
+  }
+}
+
 }  // namespace
+
+template <typename T>
+int forward_blocks_per_sm(int S, bool shared_values, size_t smem_bytes) {
+  return shared_values ? blocks_per_sm_shared<T, true>(S, smem_bytes)
+                       : blocks_per_sm_shared<T, false>(S, smem_bytes);
+}
 
 template <typename T>
 size_t forward_static_smem(int S) {
@@ -686,6 +817,8 @@ cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_
 
 template cudaError_t launch_forward<double>(const FwdParams<double>&, int, bool, size_t, cudaStream_t);
 template cudaError_t launch_forward<float>(const FwdParams<float>&, int, bool, size_t, cudaStream_t);
+template int forward_blocks_per_sm<double>(int, bool, size_t);
+template int forward_blocks_per_sm<float>(int, bool, size_t);
 template size_t forward_static_smem<double>(int);
 template size_t forward_static_smem<float>(int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);

@@ -133,11 +133,18 @@ struct PostParams {
   uint8_t* elig;
 };
 
+// Threads per forward CTA.
+constexpr int kForwardThreads = 256;
+
 template <typename T>
 cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
                            cudaStream_t stream);
 template <typename T>
 size_t forward_static_smem(int S);
+// Resident CTAs per SM of the shared-memory forward kernel with S samples per tile
+// (0 when the occupancy query fails).
+template <typename T>
+int forward_blocks_per_sm(int S, bool shared_values, size_t smem_bytes);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
 // dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0 for b < rows.

@@ -107,6 +107,43 @@ def test_forward_boundary_matches_oracle(name, index, batch, dtype, overrides):
     np.testing.assert_allclose(got["gap"], out.gap, rtol=rtol, atol=rtol)
 
 
+TILE_CASES = [
+    ("fixed-f64", np.float64, {}),
+    ("converge-f64", np.float64, {"tolerance": 1e-4, "max_iterations": 4000}),
+    ("converge-accel-f32", np.float32, {"tolerance": 1e-3, "max_iterations": 3000,
+                                        "accelerated": True}),
+    ("diag-f64", np.float64, {"diagonal_preconditioning": True}),
+]
+
+
+_TILE_ORACLE = {}
+
+
+@pytest.mark.parametrize("samples_per_tile", [1, 2, 4, 8])
+@pytest.mark.parametrize("name,dtype,overrides", TILE_CASES, ids=[c[0] for c in TILE_CASES])
+def test_forward_tile_widths_match_oracle(monkeypatch, samples_per_tile, name, dtype, overrides):
+    """Every tile width (samples per CTA), with a ragged last tile, gives the oracle's bits."""
+    monkeypatch.setenv("PURIN_CP_SAMPLES_PER_TILE", str(samples_per_tile))
+    batch = 13
+    w = make_workload(0, batch)
+    cfg = replace(w.config, **overrides)
+    if name not in _TILE_ORACLE:
+        oracle = OracleLayer(w.problem, cfg, dtype)
+        _TILE_ORACLE[name] = (oracle, oracle.solve(w.candidates, w.theta)[1])
+    oracle, saved = _TILE_ORACLE[name]
+    tdt = torch.float64 if dtype == np.float64 else torch.float32
+    layer = _layer(w.problem, cfg, batch, tdt)
+    got, _ = boundary_forward(layer, oracle, saved)
+    out = saved["out"]
+    np.testing.assert_array_equal(got["iterations"], out.iterations)
+    np.testing.assert_array_equal(got["converged"].astype(bool), out.converged)
+    np.testing.assert_array_equal(got["y"], out.y)
+    np.testing.assert_array_equal(got["dual"], out.dual)
+    np.testing.assert_array_equal(got["residual"], out.residual)
+    rtol = 1e-12 if dtype == np.float64 else 1e-5
+    np.testing.assert_allclose(got["gap"], out.gap, rtol=rtol, atol=rtol)
+
+
 @pytest.mark.parametrize("index,batch,dtype", [(0, 16, np.float64), (1, 4, np.float64),
                                                (0, 16, np.float32)])
 def test_public_solve_matches_oracle(index, batch, dtype):
