@@ -20,8 +20,8 @@ PACKAGE = HERE.parent
 ROOT = PACKAGE.parent
 LIB_DIR = PACKAGE / "_lib"
 LIB = LIB_DIR / "libpurin_cp.so"
-SOURCES = ["capi.cu", "cp_forward.cu", "cp_adjoint.cu", "cp_post.cu"]
-HEADERS = ["common.cuh", "plan.cuh", "cp_kernels.cuh"]
+SOURCES = ["capi.cu", "cp_forward.cu", "cp_adjoint.cu", "cp_post.cu", "sell_order.cu"]
+HEADERS = ["common.cuh", "plan.cuh", "cp_kernels.cuh", "sell.cuh", "sell_order.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC",

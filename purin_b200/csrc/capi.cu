@@ -18,6 +18,7 @@
 #include "../../include/purin_cp.h"
 #include "cp_kernels.cuh"
 #include "plan.cuh"
+#include "sell_order.h"
 
 namespace {
 
@@ -403,34 +404,46 @@ int32_t run_post(const PurinCpPlan* plan, const PurinCpPostArgs* a, cudaStream_t
   return PURIN_OK;
 }
 
+// Lines sorted by length, descending (stable): the sliced-ELL line order before
+// the bank-aware search.
+std::vector<int> length_order(int count, const std::vector<int32_t>& ptr) {
+  std::vector<int> order(count);
+  for (int i = 0; i < count; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return ptr[a + 1] - ptr[a] > ptr[b + 1] - ptr[b]; });
+  return order;
+}
+
 // Sliced-ELL layout (sell.cuh) of `count` lines with entries ptr_in/idx_in and slots
-// slot_in (identity when null), slices of C lines sorted by length (descending, stable).
+// slot_in (identity when null), slices of C lines in the given order (position ->
+// line); a slice is as wide as its longest line.
 struct SellHost {
   int nsl = 0;
   std::vector<int32_t> ptr, perm, idx, slot;
 };
 
 SellHost build_sell(int count, const std::vector<int32_t>& ptr_in, const std::vector<int32_t>& idx_in,
-                    const std::vector<int32_t>* slot_in, int C, int pad_index) {
+                    const std::vector<int32_t>* slot_in, int C, int pad_index,
+                    const std::vector<int>& order) {
   SellHost h;
-  std::vector<int32_t> order(count);
-  for (int i = 0; i < count; ++i) order[i] = i;
   auto len = [&](int i) { return ptr_in[i + 1] - ptr_in[i]; };
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len(a) > len(b); });
   h.nsl = (count + C - 1) / C;
   h.perm.assign((size_t)h.nsl * C, -1);
   for (int q = 0; q < count; ++q) h.perm[q] = order[q];
   h.ptr.assign(h.nsl + 1, 0);
-  for (int s = 0; s < h.nsl; ++s) h.ptr[s + 1] = h.ptr[s] + len(order[s * C]) * C;
+  for (int s = 0; s < h.nsl; ++s) {
+    int width = 0;
+    for (int q = s * C; q < std::min(count, (s + 1) * C); ++q) width = std::max(width, len(order[q]));
+    h.ptr[s + 1] = h.ptr[s] + width * C;
+  }
   h.idx.assign(h.ptr[h.nsl], pad_index);
   h.slot.assign(h.ptr[h.nsl], -1);
   for (int s = 0; s < h.nsl; ++s) {
-    const int width = (h.ptr[s + 1] - h.ptr[s]) / C;
     for (int c = 0; c < C; ++c) {
       const int q = s * C + c;
       if (q >= count) continue;
       const int line = order[q];
-      for (int k = 0; k < len(line) && k < width; ++k) {
+      for (int k = 0; k < len(line); ++k) {
         const int e = h.ptr[s] + k * C + c;
         const int src = ptr_in[line] + k;
         h.idx[e] = idx_in[src];
@@ -611,8 +624,18 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
     std::vector<SellHost> layouts;
     size_t total_sell = 0;
     const int C = 32;
-    SellHost rows_h = build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n);
-    SellHost cols_h = build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows);
+    std::vector<int> rorder = length_order(info.kept_rows, krow_ptr);
+    std::vector<int> corder = length_order(n, kcol_ptr);
+    // PURIN_CP_BANK_ORDER=0 keeps the plain length order (for comparisons).
+    const char* bank_env = std::getenv("PURIN_CP_BANK_ORDER");
+    if (!(bank_env && std::string(bank_env) == "0")) {
+      const int64_t lines = (int64_t)info.kept_rows + n;
+      const int64_t moves = std::min<int64_t>(200 * lines, 4000000);
+      purin::bank_aware_orders(info.kept_rows, n, krow_ptr, kcol, kcol_ptr, kcsc_row,
+                               (int)dtype_size(info.dtype), moves, rorder, corder);
+    }
+    SellHost rows_h = build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n, rorder);
+    SellHost cols_h = build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows, corder);
     const int m_pos = rows_h.nsl * C, n_pos = cols_h.nsl * C;
     std::vector<int32_t> pos_of_col(n + 1, n_pos), pos_of_row(info.kept_rows + 1, m_pos);
     for (int p = 0; p < n_pos; ++p)
