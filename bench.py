@@ -43,6 +43,11 @@ sys.path.insert(0, str(ROOT))
 CONFIG_INDEX = 2
 METRIC = "CP samples/sec at fixed iters (fwd+VJP)"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one cp_forward_kernel launch per sample, from the
+# ncu capture of 592 samples in profiles/cp_forward_config2_b592.md
+# ((24.70 MB + 1.3 KB) / 592); the iterates stay on chip, so the traffic is the
+# per-sample inputs and grows with the batch.
+FORWARD_DRAM_BYTES_PER_SAMPLE = (24.69888e6 + 1280.0) / 592
 
 
 def parse_args():
@@ -52,7 +57,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--batch", type=int, default=None, help="samples per GPU (default 2048)")
-    p.add_argument("--cpu-samples", type=int, default=2)
+    p.add_argument("--cpu-samples", type=int, default=6)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cp-tolerance", type=float, default=None,
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
@@ -127,6 +132,19 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def count_native_launches(step, device):
+    """Kernels of this library (namespace purin) launched by one untimed step, from the profiler."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize(device)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize(device)
+    return sum(1 for e in prof.events()
+               if e.device_type == torch.autograd.DeviceType.CUDA and "purin::" in e.name)
 
 
 def cpu_baseline_oracle(workload, samples, cores_note=1):
@@ -290,7 +308,7 @@ def main():
     per_kernel = {}
     for name, s, e in timers:
         per_kernel.setdefault(name, []).append(s.elapsed_time(e))
-    launches = len(timers)
+    launches = count_native_launches(step_device, device) * args.steps
     # Dominant kernel and its algorithmic bytes.
     with torch.no_grad():
         result = layer.solve(cand_d, theta_d)
@@ -366,7 +384,10 @@ def main():
             },
             "roofline": {
                 "bound": "hbm", "kernel": "cp_forward_kernel", "achieved": achieved,
-                "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": FORWARD_DRAM_BYTES_PER_SAMPLE * batch,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
+                                  "592 samples, scaled by samples per launch",
                 "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": fwd_bytes,
                 "launch_ms": fwd_ms,
