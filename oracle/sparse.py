@@ -65,7 +65,16 @@ class _ColumnOrder:
     def __init__(self, support, mask, n):
         flat_cols = support.reshape(-1).astype(np.int64)
         order = np.argsort(flat_cols, kind="stable")
-        counts = np.bincount(flat_cols, minlength=n)
+        # A padding contribution is +0.0, and adding +0.0 again right after one
+        # changes nothing (not even the sign of a zero sum), so each run of
+        # consecutive padding terms of a column is kept as its first term.  This
+        # keeps column 0 (where every padding slot points) short.
+        sorted_cols = flat_cols[order]
+        pad = ~mask.reshape(-1)[order]
+        repeat = np.zeros_like(pad)
+        repeat[1:] = pad[1:] & pad[:-1] & (sorted_cols[1:] == sorted_cols[:-1])
+        order = order[~repeat]  # still grouped by column, in flat order within each
+        counts = np.bincount(sorted_cols[~repeat], minlength=n)
         starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
         depth = max(1, int(counts.max(initial=0)))
         k = np.arange(depth)
