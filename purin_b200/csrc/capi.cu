@@ -110,7 +110,9 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   int64_t best_warps = -1, best_samples = -1;
   for (int S = 1, k = 0; S <= 8; S *= 2, ++k) {
     const size_t stat = f64 ? purin::forward_static_smem<double>(S) : purin::forward_static_smem<float>(S);
-    if ((size_t)S * per_sample + stat + 1024 > cap) break;
+    // Shared-memory tiles read the 16-bit index pairs (always present when a
+    // sample's state fits in shared memory).
+    if (!plan->sell[0].idx16 || (size_t)S * per_sample + stat + 1024 > cap) break;
     if (forced > 0) {
       if (S <= forced) best = S;
       continue;
@@ -420,6 +422,7 @@ std::vector<int> length_order(int count, const std::vector<int32_t>& ptr) {
 struct SellHost {
   int nsl = 0;
   std::vector<int32_t> ptr, perm, idx, slot;
+  std::vector<uint32_t> idx2;  // index pairs (sell.cuh), empty when positions need 32 bits
 };
 
 SellHost build_sell(int count, const std::vector<int32_t>& ptr_in, const std::vector<int32_t>& idx_in,
@@ -644,9 +647,27 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
       if (rows_h.perm[q] >= 0) pos_of_row[rows_h.perm[q]] = q;
     for (auto& v : rows_h.idx) v = pos_of_col[v];  // padding index n -> n_pos
     for (auto& v : cols_h.idx) v = pos_of_row[v];  // padding index m -> m_pos
+    // Index pairs (sell.cuh) when every internal position fits in 16 bits.
+    const bool idx16 = n_pos + 1 < 65536 && m_pos + 1 < 65536;
+    auto pack_pairs = [&](SellHost& h, int pad) {
+      h.idx2.assign(idx16 ? h.idx.size() : 0, 0);
+      if (!idx16) return;
+      for (int sl = 0; sl < h.nsl; ++sl) {
+        const int e0 = h.ptr[sl];
+        const int width = (h.ptr[sl + 1] - e0) / C;
+        for (int k = 0; k < width; k += 2)
+          for (int c = 0; c < C; ++c) {
+            const uint32_t lo = (uint32_t)h.idx[e0 + k * C + c];
+            const uint32_t hi = (uint32_t)(k + 1 < width ? h.idx[e0 + (k + 1) * C + c] : pad);
+            h.idx2[e0 + (k / 2) * C + c] = lo | (hi << 16);
+          }
+      }
+    };
+    pack_pairs(rows_h, n_pos);
+    pack_pairs(cols_h, m_pos);
     layouts.push_back(std::move(rows_h));
     layouts.push_back(std::move(cols_h));
-    for (auto& h : layouts) total_sell += h.ptr.size() + h.perm.size() + 2 * h.idx.size() + 64;
+    for (auto& h : layouts) total_sell += h.ptr.size() + h.perm.size() + 3 * h.idx.size() + 80;
     std::vector<int32_t> host_sell(total_sell, 0);
     std::vector<size_t> base;
     size_t at = 0;
@@ -656,6 +677,8 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
         if (!v->empty()) std::memcpy(host_sell.data() + at, v->data(), v->size() * 4);
         at += v->size() + 16;
       }
+      if (!h.idx2.empty()) std::memcpy(host_sell.data() + at, h.idx2.data(), h.idx2.size() * 4);
+      at += h.idx2.size() + 16;
     }
     DeviceGuard guard(s->device);
     cudaError_t e = cudaMalloc(&plan->sell_block, std::max<size_t>(at, 1) * sizeof(int32_t));
@@ -688,6 +711,9 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
       v.c_perm = cb + c.ptr.size() + 16;
       v.c_idx = v.c_perm + c.perm.size() + 16;
       v.c_slot = v.c_idx + c.idx.size() + 16;
+      v.idx16 = idx16 ? 1 : 0;
+      v.r_idx2 = reinterpret_cast<const uint32_t*>(v.r_slot + r.slot.size() + 16);
+      v.c_idx2 = reinterpret_cast<const uint32_t*>(v.c_slot + c.slot.size() + 16);
     }
   }
   *out = plan;

@@ -86,14 +86,33 @@ __device__ __forceinline__ void load_pack(const T* p, T (&out)[S]) {
 
 // Sliced-ELL accumulation of one lane's line for all S samples:
 // acc[q] += value_q(e) * x[index(e) * S + q] over the line's entries, in order.
-template <typename T, int S, bool kShared>
+// kPairs: indices are read two steps per 32-bit word (sell.cuh).
+template <typename T, int S, bool kShared, bool kPairs>
 struct SellLines {
   const int* ptr;
   const int* perm;
   const int* idx;
+  const uint32_t* idx2;
   const int* slot;
   const T* sell_vals;    // kShared: values in SELL order
   const T* const* vals;  // !kShared: per-sample value rows (CSR slot order)
+
+  __device__ __forceinline__ void step(int e, int col, const T* x, T (&acc)[S]) const {
+    T xs[S];
+    load_pack<T, S>(x + (size_t)col * S, xs);
+    if constexpr (kShared) {
+      const T v = __ldg(sell_vals + e);
+#pragma unroll
+      for (int q = 0; q < S; ++q) acc[q] = acc[q] + v * xs[q];
+    } else {
+      const int s0 = __ldg(slot + e);
+#pragma unroll
+      for (int q = 0; q < S; ++q) {
+        const T v = s0 >= 0 ? vals[q][s0] : T(0);
+        acc[q] = acc[q] + v * xs[q];
+      }
+    }
+  }
 
   __device__ __forceinline__ void dot(int sl, int lane, const T* x, T (&acc)[S]) const {
     const int e0 = __ldg(ptr + sl);
@@ -101,23 +120,19 @@ struct SellLines {
 #pragma unroll
     for (int q = 0; q < S; ++q) acc[q] = T(0);
     int e = e0 + lane;
-#pragma unroll 8
-    for (int k = 0; k < width; ++k, e += kC) {
-      const int col = __ldg(idx + e);
-      T xs[S];
-      load_pack<T, S>(x + (size_t)col * S, xs);
-      if constexpr (kShared) {
-        const T v = __ldg(sell_vals + e);
-#pragma unroll
-        for (int q = 0; q < S; ++q) acc[q] = acc[q] + v * xs[q];
-      } else {
-        const int s0 = __ldg(slot + e);
-#pragma unroll
-        for (int q = 0; q < S; ++q) {
-          const T v = s0 >= 0 ? vals[q][s0] : T(0);
-          acc[q] = acc[q] + v * xs[q];
-        }
+    if constexpr (kPairs) {
+      const uint32_t* w = idx2 + e0 + lane;
+      int k = 0;
+#pragma unroll 4
+      for (; k + 1 < width; k += 2, e += 2 * kC, w += kC) {
+        const uint32_t pair = __ldg(w);
+        step(e, (int)(pair & 0xffffu), x, acc);
+        step(e + kC, (int)(pair >> 16), x, acc);
       }
+      if (k < width) step(e, (int)(__ldg(w) & 0xffffu), x, acc);
+    } else {
+#pragma unroll 8
+      for (int k = 0; k < width; ++k, e += kC) step(e, __ldg(idx + e), x, acc);
     }
   }
   __device__ __forceinline__ void abs_sum(int sl, int lane, T (&acc)[S]) const {
@@ -227,8 +242,11 @@ cp_forward_kernel(const FwdParams<T> p) {
   T* dv = av + (size_t)(n_pos + 1) * S;
   T* sv_ = dv + (size_t)(n_pos + 1) * S;
 
-  const SellLines<T, S, kShared> rows{sv.r_ptr, sv.r_perm, sv.r_idx, sv.r_slot, p.vr, vals_q};
-  const SellLines<T, S, kShared> cols{sv.c_ptr, sv.c_perm, sv.c_idx, sv.c_slot, p.vc, vals_q};
+  // Shared-memory tiles read index pairs (positions fit in 16 bits there).
+  const SellLines<T, S, kShared, kSmem> rows{sv.r_ptr, sv.r_perm, sv.r_idx, sv.r_idx2, sv.r_slot,
+                                              p.vr, vals_q};
+  const SellLines<T, S, kShared, kSmem> cols{sv.c_ptr, sv.c_perm, sv.c_idx, sv.c_idx2, sv.c_slot,
+                                              p.vc, vals_q};
   const T zero = T(0), one = T(1);
   const T safety = p.safety;
 

@@ -16,6 +16,13 @@
 // terms.  Within a line entries keep their original order (CSR order for rows;
 // ascending row, i.e. the reference scatter's update order, for columns), so
 // sums round exactly as the reference's sequential accumulation.
+//
+// When every internal position fits in 16 bits (idx16), the indices are also
+// stored in pairs: the 32-bit word at ptr[s] + (k / 2) * 32 + lane, for even k,
+// holds the positions of steps k (low half) and k + 1 (high half; the padding
+// position when k + 1 == width(s)), so a warp reads the indices of two steps
+// in one 128-byte request.  Only the first half of each slice's word range is
+// used, which keeps the word index a function of ptr[s] alone.
 #pragma once
 
 #include <stdint.h>
@@ -35,6 +42,9 @@ struct SellView {
   const int* c_perm;     // n_pos: variable of each internal column position, -1 for padding
   const int* c_idx;      // nnz_c: internal row position, m_pos for padding
   const int* c_slot;     // nnz_c: kept CSR slot, -1 for padding
+  int idx16;                  // 1: r_idx2 / c_idx2 are present
+  const uint32_t* r_idx2;     // nnz_r words: r_idx in pairs of steps (see above)
+  const uint32_t* c_idx2;     // nnz_c words: c_idx in pairs of steps
 };
 
 }  // namespace purin
