@@ -633,7 +633,9 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
     const char* bank_env = std::getenv("PURIN_CP_BANK_ORDER");
     if (!(bank_env && std::string(bank_env) == "0")) {
       const int64_t lines = (int64_t)info.kept_rows + n;
-      const int64_t moves = std::min<int64_t>(200 * lines, 4000000);
+      int64_t moves = std::min<int64_t>(200 * lines, 1000000);
+      // PURIN_CP_BANK_MOVES overrides the search budget (for comparisons).
+      if (const char* env = std::getenv("PURIN_CP_BANK_MOVES")) moves = std::atoll(env);
       purin::bank_aware_orders(info.kept_rows, n, krow_ptr, kcol, kcol_ptr, kcsc_row,
                                (int)dtype_size(info.dtype), moves, rorder, corder);
     }
