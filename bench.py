@@ -45,9 +45,9 @@ METRIC = "CP samples/sec at fixed iters (fwd+VJP)"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one cp_forward_kernel launch per sample, from the
 # ncu capture of 592 samples in profiles/cp_forward_config2_b592.md
-# ((24.70 MB + 1.3 KB) / 592); the iterates stay on chip, so the traffic is the
+# ((24.72 MB + 11.5 KB) / 592); the iterates stay on chip, so the traffic is the
 # per-sample inputs and grows with the batch.
-FORWARD_DRAM_BYTES_PER_SAMPLE = (24.69888e6 + 1280.0) / 592
+FORWARD_DRAM_BYTES_PER_SAMPLE = (24.716288e6 + 11520.0) / 592
 
 
 def parse_args():
