@@ -18,8 +18,9 @@ theta = [b; h]).  One step = forward + VJP over the whole batch.
   of the loss and both gradients inside the timed region.
 * ``roofline``: the dominant kernel's algorithmic bytes per launch divided by
   its event-timed launch duration, against MEASURED_PEAKS.json.
-* ``cpu_baseline``: the NumPy oracle (a restatement of the reference's JAX
-  path; JAX itself is not installed on the host) on a bounded sample.
+* ``cpu_baseline``: the oracle (a restatement of the reference's JAX path; JAX
+  itself is not installed on the host) on a bounded sample, its CP loop in C++
+  over every host core.
 """
 
 from __future__ import annotations
@@ -57,7 +58,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--batch", type=int, default=None, help="samples per GPU (default 2048)")
-    p.add_argument("--cpu-samples", type=int, default=6)
+    p.add_argument("--cpu-samples", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cp-tolerance", type=float, default=None,
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
@@ -147,22 +148,36 @@ def count_native_launches(step, device):
                if e.device_type == torch.autograd.DeviceType.CUDA and "purin::" in e.name)
 
 
-def cpu_baseline_oracle(workload, samples, cores_note=1):
-    """Time the NumPy oracle (fwd + VJP) on the first ``samples`` samples."""
+def _native_oracle(workload, threads):
+    """The oracle with its CP loop in C++ on ``threads`` host threads (checker-only code)."""
     sys.path.insert(0, str(ROOT / "tests"))
     from helpers import OracleLayer  # noqa: E402  (test infrastructure, checker only)
 
+    from oracle.cpu import sparse_cp_native
+
     layer = OracleLayer(workload.problem, workload.config, np.float64)
-    cand = workload.candidates[:samples]
-    theta = workload.theta[:samples]
-    targets = workload.targets[:samples]
+    layer.proj.cp_solver = lambda *a, **k: sparse_cp_native(*a, threads=threads, **k)
+    return layer
+
+
+def _oracle_step(layer, workload, sl, total):
+    result, saved = layer.solve(workload.candidates[sl], workload.theta[sl],
+                                offset=sl.start or 0, total=total)
+    layer.proj.vjp(saved, result["y"] - workload.targets[sl])
+
+
+def cpu_baseline_oracle(workload, samples):
+    """Time the oracle (fwd with the C++ CP loop on every host core + NumPy VJP)."""
+    cores = len(os.sched_getaffinity(0))
+    layer = _native_oracle(workload, cores)
+    samples = min(samples, workload.candidates.shape[0])
     t0 = time.perf_counter()
-    result, saved = layer.solve(cand, theta, total=workload.candidates.shape[0])
-    layer.proj.vjp(saved, result["y"] - targets)
+    _oracle_step(layer, workload, slice(0, samples), workload.candidates.shape[0])
     elapsed = time.perf_counter() - t0
-    return {"value": samples / elapsed, "unit": "samples/s", "cores": cores_note, "kind": "port",
-            "sample": f"{samples} samples of config 2 (fwd 2000 it + VJP), NumPy oracle, "
-                      f"{elapsed:.1f} s"}
+    return {"value": samples / elapsed, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{samples} samples of config 2 (fwd 2000 it + VJP) in {elapsed:.1f} s: "
+                      f"the CP loop restated in C++ (OpenMP, {cores} threads), presolve, "
+                      "post-processing and VJP in the NumPy restatement"}
 
 
 def run_reference(args):
@@ -170,21 +185,18 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import multiprocessing as mp
-
     from purin_b200.workloads import make_workload
 
     cores = len(os.sched_getaffinity(0))
-    per_step = max(1, min(cores, 8))
+    per_step = 8 * cores
     workload = make_workload(CONFIG_INDEX, per_step)
-    ctx = mp.get_context("spawn")
+    layer = _native_oracle(workload, cores)
     times = []
-    with ctx.Pool(per_step) as pool:
-        for step in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            pool.map(_reference_sample, [(i, per_step) for i in range(per_step)])
-            if step >= args.warmup:
-                times.append(time.perf_counter() - t0)
+    for step in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        _oracle_step(layer, workload, slice(0, per_step), per_step)
+        if step >= args.warmup:
+            times.append(time.perf_counter() - t0)
     ms = 1000.0 * statistics.mean(times)
     value = per_step / (ms / 1000.0)
     line = {
@@ -194,31 +206,15 @@ def run_reference(args):
         "data": "synthetic (seeded generator of benchmark configuration 2)",
         "config": {"workload": "config2: fp64 n=2048 me=512 mi=1024 8nnz/row, 2000 it, fwd+VJP",
                    "samples_per_step": per_step},
-        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": per_step, "kind": "port",
-                         "sample": f"{per_step} samples per step, one per process"},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": cores, "kind": "port",
+                         "sample": f"{per_step} samples per step: CP loop in C++ (OpenMP, "
+                                   f"{cores} threads), NumPy presolve, post-processing and VJP"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "JAX is not installed on this host; the reference's own CPU path cannot run. "
-                "This arm times the NumPy restatement of that path (oracle/).",
+                "This arm times the CPU restatement of that path (oracle/).",
     }
     print(json.dumps(line), flush=True)
-
-
-def _reference_sample(arg):
-    index, total = arg
-    sys.path.insert(0, str(ROOT))
-    sys.path.insert(0, str(ROOT / "tests"))
-    from helpers import OracleLayer
-
-    from purin_b200.workloads import make_workload
-
-    workload = make_workload(CONFIG_INDEX, total)
-    layer = OracleLayer(workload.problem, workload.config, np.float64)
-    sl = slice(index, index + 1)
-    result, saved = layer.solve(workload.candidates[sl], workload.theta[sl], offset=index,
-                                total=total)
-    layer.proj.vjp(saved, result["y"] - workload.targets[sl])
-    return 0
 
 
 def main():
@@ -365,7 +361,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_oracle(workload, args.cpu_samples)
+        cpu = cpu_baseline_oracle(make_workload(CONFIG_INDEX, args.cpu_samples),
+                                  args.cpu_samples)
 
     if rank == 0:
         line = {

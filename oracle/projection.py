@@ -84,6 +84,9 @@ class OracleProjection:
         self.support = self.support_all[self.rows]
         self.mask = self.mask_all[self.rows]
         self.partitionable = partitionable
+        # The CP loop (oracle.cp.sparse_cp; oracle.cpu.sparse_cp_native runs the
+        # same loop in C++ on the host cores).
+        self.cp_solver = sparse_cp
 
     # -- forward -------------------------------------------------------------
     def presolve(self, values, rhs, target):
@@ -132,7 +135,7 @@ class OracleProjection:
         tolerance = dtype.type(cfg.tolerance) * np.minimum(dtype.type(1.0), min_scale)
         data = kept * scale[:, :, None]
         scaled_rhs = rhs[:, self.rows] * scale
-        out = sparse_cp(
+        out = self.cp_solver(
             np.ones_like(target), -target, data, scaled_rhs, self.support, self.mask,
             self.me, lower, upper, accelerated=cfg.accelerated, safety=cfg.safety,
             max_iterations=cfg.max_iterations, tolerance=tolerance,
