@@ -58,7 +58,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--batch", type=int, default=None, help="samples per GPU (default 2048)")
-    p.add_argument("--cpu-samples", type=int, default=256)
+    p.add_argument("--cpu-samples", type=int, default=None,
+                   help="samples in the CPU baseline (default 48 per host core, ~15 s)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cp-tolerance", type=float, default=None,
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
@@ -361,8 +362,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_oracle(make_workload(CONFIG_INDEX, args.cpu_samples),
-                                  args.cpu_samples)
+        samples = args.cpu_samples or 48 * len(os.sched_getaffinity(0))
+        cpu = cpu_baseline_oracle(make_workload(CONFIG_INDEX, samples), samples)
 
     if rank == 0:
         line = {
