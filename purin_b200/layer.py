@@ -318,8 +318,10 @@ class PreparedChambollePockProjection:
         if self._n_bound == 0:
             feasible = torch.ones((batch,), dtype=torch.uint8, device=dev)
             return lower, upper, feasible, None, None
-        coefficient = values[:, self._bound_slots].expand(rows_b, -1)
-        b_rhs = rhs[:rows_b, self._bound_rows].expand(rows_b, -1)
+        # index_select for gathers by unique indices: its gradient writes each
+        # element once (no sort-based accumulation).
+        coefficient = torch.index_select(values, 1, self._bound_slots).expand(rows_b, -1)
+        b_rhs = torch.index_select(rhs[:rows_b], 1, self._bound_rows).expand(rows_b, -1)
         threshold = b_rhs / torch.where(coefficient != 0, coefficient, torch.ones_like(coefficient))
         index = self._bound_vars.unsqueeze(0).expand(rows_b, -1)
         lower = lower.scatter_reduce(1, index, torch.where(coefficient < 0, threshold, -inf), "amax",
@@ -354,7 +356,7 @@ class PreparedChambollePockProjection:
         if rhs.shape[0] != batch:
             rhs = rhs.expand(batch, -1)
         lower, upper, feasible, coefficient, threshold = self._presolve(values, rhs, batch)
-        kept = values[:, self._kept_slots]
+        kept = torch.index_select(values, 1, self._kept_slots)
         scale = self._row_scale(kept)
         eq = (torch.zeros((batch, me), dtype=dt, device=dev) if multipliers_eq is None
               else torch.as_tensor(multipliers_eq, dtype=dt, device=dev))
@@ -369,7 +371,7 @@ class PreparedChambollePockProjection:
                      else torch.ones((batch,), dtype=dt, device=dev))
         tolerance = (self.config.tolerance * torch.clamp_max(min_scale, 1.0)).detach().contiguous()
         data = (kept * scale[:, self._slot_row]).contiguous()
-        scaled_rhs = (rhs[:, self._kept_rows] * scale_b).contiguous()
+        scaled_rhs = (torch.index_select(rhs, 1, self._kept_rows) * scale_b).contiguous()
         out = _CPOut(*_SolveFunction.apply(data, scaled_rhs, target.contiguous(),
                                            lower.contiguous(), upper.contiguous(), initial,
                                            tolerance, feasible, self))

@@ -546,7 +546,11 @@ class _MatrixCanonical(CanonicalAffine):
             mask = self._const("mask", self._map_mask, theta)
             acc = None
             for k in range(self._map_width):
-                term = theta[:, idx[:, k]] * val[None, :, k]
+                # Masked slots repeat index 0 with a zero term, so a gather whose
+                # gradient adds into each parameter in any order is exact.
+                gathered = (theta[:, idx[:, k]] if xp is np
+                            else xp.index_select(theta, 1, idx[:, k].contiguous()))
+                term = gathered * val[None, :, k]
                 term = xp.where(mask[None, :, k], term, xp.zeros_like(term))
                 acc = term if acc is None else acc + term
             rhs = rhs + acc
