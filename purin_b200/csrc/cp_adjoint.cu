@@ -276,7 +276,18 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
   const unsigned nblocks = gridDim.x;
 
   // ---- phase 0: step sizes, linearisation, right-hand side ----------------
+  // A sample whose forward solve did not converge has right-hand side
+  // g = (where(converged, cot, 0), 0, 0) = 0 (bounds.py:133), so x = 0 solves its
+  // system exactly and its gradients are zeros (bounds.py:148-165): it is not
+  // linearised, never enters GMRES and gets zeros in the final phase.
   for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+    if (p.converged[X] == 0) {
+      if (threadIdx.x == 0) {
+        p.thresh[X] = pmax(p.lin_atol, zero);
+        p.resinf[X] = zero;
+      }
+      continue;
+    }
     const T* vals = p.values + X * p.values_stride;
     if (p.diag) {
       T* base = p.dsteps + X * (2 * (int64_t)n + m);
@@ -525,6 +536,23 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
 
   // ---- validity and parameter pullback (bounds.py:148-165) ------------------
   for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+    if (p.converged[X] == 0) {
+      // Zero right-hand side: zero solution (status 0, residual 0), zero gradients.
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        if (p.g_target) p.g_target[X * n + j] = zero;
+        if (p.g_lower) p.g_lower[X * n + j] = zero;
+        if (p.g_upper) p.g_upper[X * n + j] = zero;
+      }
+      for (int i = threadIdx.x; i < m; i += kThreads)
+        if (p.g_rhs) p.g_rhs[X * m + i] = zero;
+      if (p.g_values)
+        for (int k = threadIdx.x; k < st.nnz; k += kThreads) p.g_values[X * st.nnz + k] = zero;
+      if (threadIdx.x == 0) {
+        if (p.lin_status) p.lin_status[X] = 0;
+        if (p.lin_residual) p.lin_residual[X] = zero;
+      }
+      continue;
+    }
     const Sample<T> s = make_sample(p, X);
     const T* x = p.x + X * W;
     int fin = 1;
