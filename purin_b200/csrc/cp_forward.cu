@@ -410,9 +410,12 @@ cp_forward_kernel(const FwdParams<T> p) {
   // Phase A: dual update; with kFull also the dual objective term rhs . lambda+.
   auto phase_a = [&](auto full_c, int act, int& fin) {
     constexpr bool kFull = decltype(full_c)::value;
-    T rd[S];
+    T rd[S], sigma[S];
 #pragma unroll
-    for (int q = 0; q < S; ++q) rd[q] = zero;
+    for (int q = 0; q < S; ++q) {
+      rd[q] = zero;
+      sigma[q] = sc.sigma[q];  // per-sample scalars of this iteration, read once
+    }
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
       const int i = rows.line(sl, lane);
       const int qp = sl * kC + lane;
@@ -428,7 +431,7 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
         for (int q = 0; q < S; ++q) {
           if (!((act >> q) & 1)) continue;
-          const T sg = p.diag ? sv_[(size_t)qp * S + q] : sc.sigma[q];
+          const T sg = p.diag ? sv_[(size_t)qp * S + q] : sigma[q];
           const T raw = lv[q] + sg * (acc[q] - rbs[q]);
           const T nl = i < me ? raw : pmax(raw, zero);
           lv[q] = nl;
@@ -444,9 +447,14 @@ cp_forward_kernel(const FwdParams<T> p) {
   // violation and the primal and dual objectives of y+.
   auto phase_b = [&](auto full_c, int act, int& fin) {
     constexpr bool kFull = decltype(full_c)::value;
-    T stm[S], resm[S], ps[S], ds[S];
+    T stm[S], resm[S], ps[S], ds[S], a_s[S], d_s[S], theta_s[S];
 #pragma unroll
-    for (int q = 0; q < S; ++q) stm[q] = resm[q] = ps[q] = ds[q] = zero;
+    for (int q = 0; q < S; ++q) {
+      stm[q] = resm[q] = ps[q] = ds[q] = zero;
+      a_s[q] = sc.a[q];  // per-sample scalars of this iteration, read once
+      d_s[q] = sc.d[q];
+      theta_s[q] = sc.theta[q];
+    }
     for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
       const int j = cols.line(sl, lane);
       const int pp = sl * kC + lane;
@@ -470,15 +478,15 @@ cp_forward_kernel(const FwdParams<T> p) {
           const size_t js = (size_t)pp * S + q;
           const T yo = yv[q];
           const T c = -tg[q];
-          const T aa = p.diag ? av[js] : sc.a[q];
-          const T dd = p.diag ? dv[js] : sc.d[q];
+          const T aa = p.diag ? av[js] : a_s[q];
+          const T dd = p.diag ? dv[js] : d_s[q];
           const T off = (-dd) * c;
           const T yr = (aa * yo - dd * t[q]) + off;
           const T l = lb[q];
           const T u = ub[q];
           const T yn = clip(yr, l, u);
           yv[q] = yn;
-          bv[q] = yn + sc.theta[q] * (yn - yo);
+          bv[q] = yn + theta_s[q] * (yn - yo);
           if (!finite(yn)) fin &= ~(1 << q);
           if constexpr (kFull) {
             resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
