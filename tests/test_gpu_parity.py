@@ -254,3 +254,34 @@ def test_autograd_chain_matches_fd():
                 ym = layer(_t(args_m[0], torch.float64), _t(args_m[1], torch.float64))
                 fd[b, i] = float(((yp - ym) * g).sum()) / (2 * eps)
         np.testing.assert_allclose(grad.cpu().numpy(), fd, atol=2e-6, err_msg=which)
+
+
+def test_parameter_dependent_coefficients_per_sample():
+    """Coefficients that depend on the parameters differ per sample: the per-sample
+    values path of the forward kernel through the public API (presolve, row scaling,
+    bound rows whose coefficient is a parameter)."""
+    from purin_b200.problems import Projection
+
+    p = Projection()
+    t = p.add_parameter(["a", "b", "c", "d"])
+    y = p.add_variable(["u", "v", "w", "z"])
+    p.objective = 0.0
+    p.constraints.add(t.a * y.u + y.v - y.w == t.b)
+    p.constraints.add(y.u + t.c * y.w + y.z <= 1.5)
+    p.constraints.add(y.v - y.z >= -t.d)
+    p.constraints.add(t.c * y.z <= 2.0)  # singleton row with a parameter coefficient
+    p.constraints.add(y.u >= -1.0, y.u <= 1.0, y.w >= -2.0)
+    batch = 8
+    rng = np.random.default_rng(7)
+    theta = np.column_stack([rng.uniform(0.5, 2.0, batch), rng.normal(size=batch),
+                             rng.uniform(0.5, 2.0, batch), rng.uniform(0.0, 1.0, batch)])
+    candidates = 2.0 * rng.normal(size=(batch, 4))
+    cfg = ChambollePockConfig(max_iterations=400)
+    oracle = OracleLayer(p, cfg, np.float64)
+    expected, _ = oracle.solve(candidates, theta)
+    layer = _layer(p, cfg, batch, torch.float64)
+    got = layer.solve(_t(candidates, torch.float64), _t(theta, torch.float64))
+    for field in ("y", "multipliers_eq", "multipliers_ineq", "slacks", "residual_inf_norm",
+                  "status", "iterations"):
+        np.testing.assert_array_equal(getattr(got, field).cpu().numpy(), expected[field],
+                                      err_msg=field)
