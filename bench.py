@@ -43,6 +43,17 @@ sys.path.insert(0, str(ROOT))
 
 CONFIG_INDEX = 2
 METRIC = "CP samples/sec at fixed iters (fwd+VJP)"
+DEFAULT_BATCH = {0: 256, 1: 4096, 2: 2048, 3: 2048, 4: 16384}
+WORKLOADS = {
+    0: "config0: fp64, n=64, me=32, mi=32, 4 nnz/row, |y|<=1, 500 fixed-step CP iterations",
+    1: "config1: n=1024, me=256, mi=512, 8 nnz/row, box bounds, 1000 accelerated CP iterations",
+    2: "config2: fp64, n=2048, me=512, mi=1024, 8 nnz/row, box bounds, 2000 fixed-step CP "
+       "iterations",
+    3: "config3: fp32 network flow, 5000 nodes, 20000 edges, 4000 coupling rows, capacity "
+       "bounds, 1500 fixed-step CP iterations",
+    4: "config4: WeightedDistance w~U(0.5,2), n=4096, me=1024, mi=2048, 16 nnz/row, box bounds, "
+       "1000 accelerated CP iterations",
+}
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one cp_forward_kernel launch per sample, from the
 # ncu capture of 592 samples in profiles/cp_forward_config2_b592.md
@@ -57,7 +68,15 @@ def parse_args():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
-    p.add_argument("--batch", type=int, default=None, help="samples per GPU (default 2048)")
+    p.add_argument("--batch", type=int, default=None,
+                   help="samples per GPU (default: 2048 for configs 2 and 3, 4096 for config 1, "
+                        "16384 for config 4, 256 for config 0)")
+    p.add_argument("--config", type=int, default=CONFIG_INDEX, choices=[0, 1, 2, 3, 4],
+                   help="benchmark configuration (the headline is configuration 2)")
+    p.add_argument("--mode", default=None, choices=["fwd", "fwd+vjp"],
+                   help="forward only or forward + VJP (default: fwd+vjp for config 2, else fwd)")
+    p.add_argument("--dtype", default=None, choices=["float64", "float32"],
+                   help="override the configuration's dtype")
     p.add_argument("--cpu-samples", type=int, default=None,
                    help="samples in the CPU baseline (default 48 per host core, ~15 s)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -246,25 +265,35 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(device)
 
-    batch = args.batch or 2048
+    index = args.config
+    vjp = (args.mode or ("fwd+vjp" if index == CONFIG_INDEX else "fwd")) == "fwd+vjp"
+    batch = args.batch or DEFAULT_BATCH[index]
     total = batch * world
-    workload = make_workload(CONFIG_INDEX, batch, seed=rank)
+    workload = make_workload(index, batch, seed=rank, dtype=args.dtype)
+    tdt = torch.float64 if workload.dtype == "float64" else torch.float32
     cfg = workload.config
+    if workload.weights is not None:  # configuration 4: WeightedDistance
+        cfg = dataclasses.replace(cfg, metric_diagonal=tuple(float(v) for v in workload.weights))
     if args.cp_tolerance is not None:
         cfg = dataclasses.replace(cfg, tolerance=args.cp_tolerance)
     layer = prepare_projection(workload.problem, method="chambolle-pock", config=cfg,
-                               batch_size=batch, dtype=torch.float64, backend=str(device))
+                               batch_size=batch, dtype=tdt, backend=str(device))
     layer.set_shard(rank * batch, total)
     n = workload.problem.variable_size
     m = layer._m
-    w = 8
+    w = 8 if tdt == torch.float64 else 4
 
-    cand_d = torch.as_tensor(workload.candidates, device=device)
-    theta_d = torch.as_tensor(workload.theta, device=device)
-    targ_d = torch.as_tensor(workload.targets, device=device)
+    cand_d = torch.as_tensor(workload.candidates, dtype=tdt, device=device)
+    theta_d = torch.as_tensor(workload.theta, dtype=tdt, device=device)
+    targets = (workload.targets if workload.targets is not None
+               else np.random.default_rng(1000 + rank).normal(size=(batch, n)))
+    targ_d = torch.as_tensor(targets, dtype=tdt, device=device)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def step_device(timers=None):
+        if not vjp:
+            with torch.no_grad():
+                return layer(cand_d, theta_d)
         x = cand_d.detach().requires_grad_(True)
         th = theta_d.detach().requires_grad_(True)
         y = layer(x, th)
@@ -319,14 +348,20 @@ def main():
     eligible = int(result.gradient_eligible.sum().item())
 
     # ---- end-to-end through the public API from pinned host buffers ---------------
-    cand_h = torch.as_tensor(workload.candidates).pin_memory()
-    theta_h = torch.as_tensor(workload.theta).pin_memory()
-    targ_h = torch.as_tensor(workload.targets).pin_memory()
+    cand_h = torch.as_tensor(workload.candidates, dtype=tdt).pin_memory()
+    theta_h = torch.as_tensor(workload.theta, dtype=tdt).pin_memory()
+    targ_h = torch.as_tensor(targets, dtype=tdt).pin_memory()
     gx_h = torch.empty_like(cand_h).pin_memory()
     gth_h = torch.empty_like(theta_h).pin_memory()
-    loss_h = torch.empty((), dtype=torch.float64).pin_memory()
+    loss_h = torch.empty((), dtype=tdt).pin_memory()
 
     def step_e2e():
+        if not vjp:  # forward only: candidates and parameters in, projections out
+            with torch.no_grad():
+                y = layer(cand_h.to(device, non_blocking=True),
+                          theta_h.to(device, non_blocking=True))
+                gx_h.copy_(y, non_blocking=True)
+            return
         x = cand_h.to(device, non_blocking=True).requires_grad_(True)
         th = theta_h.to(device, non_blocking=True).requires_grad_(True)
         t = targ_h.to(device, non_blocking=True)
@@ -334,7 +369,8 @@ def main():
         loss = 0.5 * ((y - t) ** 2).sum()
         loss.backward()
         gx_h.copy_(x.grad, non_blocking=True)
-        gth_h.copy_(th.grad, non_blocking=True)
+        if th.grad is not None:  # configurations that differentiate the parameters
+            gth_h.copy_(th.grad, non_blocking=True)
         loss_h.copy_(loss.detach(), non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
@@ -357,25 +393,34 @@ def main():
         t = torch.tensor([e2e_local], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e = float(t.item())
-    h2d = (cand_h.numel() + theta_h.numel() + targ_h.numel()) * 8
-    d2h = (gx_h.numel() + gth_h.numel() + 1) * 8
+    if vjp:
+        h2d = (cand_h.numel() + theta_h.numel() + targ_h.numel()) * w
+        theta_grad = cfg.implicit_gradient.differentiate_problem_parameters
+        d2h = (gx_h.numel() + (gth_h.numel() if theta_grad else 0) + 1) * w
+    else:
+        h2d = (cand_h.numel() + theta_h.numel()) * w
+        d2h = gx_h.numel() * w
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    headline = index == CONFIG_INDEX and vjp and tdt == torch.float64
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and headline:
         samples = args.cpu_samples or 48 * len(os.sched_getaffinity(0))
         cpu = cpu_baseline_oracle(make_workload(CONFIG_INDEX, samples), samples)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
+            "metric": METRIC if vjp else METRIC.replace("(fwd+VJP)", "(fwd)"), "value": value,
+            "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (seeded generator of benchmark configuration 2; no dataset)",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64" if w == 8 else "f32",
+            "data": f"synthetic (seeded generator of benchmark configuration {index}; no dataset)",
             "config": {
-                "workload": "config2: fp64, n=2048, me=512, mi=1024, 8 nnz/row, box bounds, "
-                            f"2000 fixed-step CP iterations (tolerance {cfg.tolerance:g} "
-                            "stopping test kept), fwd + implicit VJP w.r.t. candidates and "
-                            "parameters",
+                "workload": WORKLOADS[index].replace(
+                    "config1: ", f"config1: {'fp64' if w == 8 else 'fp32'}, ").replace(
+                    "config4: ", f"config4: {'fp64' if w == 8 else 'fp32'}, ")
+                + f" (tolerance {cfg.tolerance:g} stopping test kept), "
+                + ("fwd + implicit VJP w.r.t. candidates and parameters" if vjp else "forward"),
                 "samples_per_gpu": batch, "global_batch": total,
                 "l2": "flushed between timed steps (256 MB write outside the step events)",
                 "gradient_eligible": f"{eligible}/{batch} on rank 0",
@@ -383,9 +428,11 @@ def main():
             "roofline": {
                 "bound": "hbm", "kernel": "cp_forward_kernel", "achieved": achieved,
                 "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": FORWARD_DRAM_BYTES_PER_SAMPLE * batch,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at "
-                                  "592 samples, scaled by samples per launch",
+                "traffic": FORWARD_DRAM_BYTES_PER_SAMPLE * batch if index == CONFIG_INDEX
+                else None,
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                   "at 592 samples, scaled by samples per launch")
+                if index == CONFIG_INDEX else None,
                 "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": fwd_bytes,
                 "launch_ms": fwd_ms,
