@@ -55,6 +55,7 @@ constexpr uint64_t kBarrierTimeoutNs = 60ull * 1000ull * 1000ull * 1000ull;
 // Forward tile plan: samples per CTA and whether the tile state fits in shared memory.
 struct FwdPlan {
   int S = 1;
+  int NT = purin::kForwardThreads;  // threads per CTA
   bool smem = true;
   size_t smem_bytes = 0;
   size_t workspace = 0;  // total bytes
@@ -100,46 +101,57 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
       (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
-  // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it fits.
-  int forced = 0;
+  // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
+  // fits, PURIN_CP_TILE_THREADS (256 or 1024) the threads per CTA.
+  int forced = 0, forced_threads = 0;
   if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
-  // Default: the tile width whose resident CTAs hold the most warps over the
-  // batch (the iteration is latency-bound), then the most samples, then the
-  // narrowest.  Every width whose state fits in shared memory is a candidate.
-  int best = 0;
+  if (const char* env = std::getenv("PURIN_CP_TILE_THREADS")) forced_threads = std::atoi(env);
+  // Default: the shape whose resident CTAs hold the most warps over the batch
+  // (the iteration is latency-bound), then the most samples, then the first of
+  // this list.  Every shape whose state fits in shared memory is a candidate.
+  static const int kShapes[5][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
+                                    {4, purin::kForwardThreads}, {8, purin::kForwardThreads},
+                                    {1, purin::kWideThreads}};
+  int best = -1;
   int64_t best_warps = -1, best_samples = -1;
-  for (int S = 1, k = 0; S <= 8; S *= 2, ++k) {
-    const size_t stat = f64 ? purin::forward_static_smem<double>(S) : purin::forward_static_smem<float>(S);
+  for (int k = 0; k < 5; ++k) {
+    const int S = kShapes[k][0], NT = kShapes[k][1];
+    const size_t stat = f64 ? purin::forward_static_smem<double>(S, NT)
+                            : purin::forward_static_smem<float>(S, NT);
     // Shared-memory tiles read the 16-bit index pairs (always present when a
     // sample's state fits in shared memory).
-    if (!plan->sell[0].idx16 || (size_t)S * per_sample + stat + 1024 > cap) break;
-    if (forced > 0) {
-      if (S <= forced) best = S;
+    if (!plan->sell[0].idx16 || (size_t)S * per_sample + stat + 1024 > cap) continue;
+    if (forced > 0 || forced_threads > 0) {
+      const int want_s = forced > 0 ? forced : 8;
+      const int want_nt = forced_threads > 0 ? forced_threads : purin::kForwardThreads;
+      if (NT == want_nt && S <= want_s && (best < 0 || S > kShapes[best][0])) best = k;
       continue;
     }
     int& cached = plan->fwd_blocks[diag ? 1 : 0][shared_values ? 1 : 0][k];
     if (cached < 0) {
       const size_t dyn = (size_t)S * per_sample;
-      cached = f64 ? purin::forward_blocks_per_sm<double>(S, shared_values, dyn)
-                   : purin::forward_blocks_per_sm<float>(S, shared_values, dyn);
+      cached = f64 ? purin::forward_blocks_per_sm<double>(S, NT, shared_values, dyn)
+                   : purin::forward_blocks_per_sm<float>(S, NT, shared_values, dyn);
     }
     const int64_t tiles = (batch + S - 1) / S;
     const int64_t ctas = std::min<int64_t>(tiles, sms * std::max(cached, 0));
-    const int64_t warps = ctas * (purin::kForwardThreads / 32);
+    const int64_t warps = ctas * (NT / 32);
     const int64_t samples = std::min<int64_t>(batch, ctas * S);
-    if (best == 0 || warps > best_warps || (warps == best_warps && samples > best_samples)) {
-      best = S;
+    if (best < 0 || warps > best_warps || (warps == best_warps && samples > best_samples)) {
+      best = k;
       best_warps = warps;
       best_samples = samples;
     }
   }
-  if (best > 0) {
-    fp.S = best;
+  if (best >= 0) {
+    fp.S = kShapes[best][0];
+    fp.NT = kShapes[best][1];
     fp.smem = true;
-    fp.smem_bytes = (size_t)best * per_sample;
+    fp.smem_bytes = (size_t)fp.S * per_sample;
     fp.workspace = 0;
   } else {
     fp.S = 8;
+    fp.NT = purin::kForwardThreads;
     fp.smem = false;
     fp.smem_bytes = 0;
     const int64_t tiles = (batch + fp.S - 1) / fp.S;
@@ -302,7 +314,7 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.sell = sv;
   p.vr = vr;
   p.vc = vc;
-  cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.smem, fp.smem_bytes, stream);
+  cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.NT, fp.smem, fp.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward launch");
   return PURIN_OK;
 }

@@ -40,11 +40,9 @@ namespace purin {
 
 namespace {
 
-constexpr int kThreads = kForwardThreads;
-constexpr int kWarps = kThreads / 32;
 constexpr int kC = 32;  // sliced-ELL slice height: one row per lane
 
-template <typename T, int S>
+template <typename T, int S, int kWarps>
 struct TileScratch {
   T tau[S], sigma[S], theta[S], a[S], d[S], tol[S];
   T res_out[S], gap_out[S];
@@ -170,7 +168,7 @@ __device__ __forceinline__ T warp_max32(T v) {
 }
 
 // Per-sample tile reductions; every thread receives all S totals.
-template <typename T, int S, bool kMax>
+template <typename T, int S, bool kMax, int kWarps>
 __device__ __forceinline__ void tile_reduce(T (&v)[S], T (&scratch)[kWarps][S]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -184,7 +182,7 @@ __device__ __forceinline__ void tile_reduce(T (&v)[S], T (&scratch)[kWarps][S]) 
 #pragma unroll
   for (int q = 0; q < S; ++q) {
     T total = T(0);
-#pragma unroll
+#pragma unroll 8
     for (int w = 0; w < kWarps; ++w) total = kMax ? pmax(total, scratch[w][q]) : total + scratch[w][q];
     v[q] = total;
   }
@@ -209,11 +207,19 @@ __device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
   }
 }
 
-template <typename T, int S, bool kSmem, bool kShared>
-__global__ void __launch_bounds__(kThreads, (S == 1) ? 4 : (S <= 2) ? 2 : 1)
+// Resident CTAs per SM the register budget is sized for: one 1024-thread CTA,
+// or 4 / 2 / 1 CTAs of 256 threads for S = 1 / 2 / wider.
+constexpr int forward_min_blocks(int S, int NT) {
+  return NT > kForwardThreads ? 1 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
+}
+
+template <typename T, int S, int NT, bool kSmem, bool kShared>
+__global__ void __launch_bounds__(NT, forward_min_blocks(S, NT))
 cp_forward_kernel(const FwdParams<T> p) {
+  constexpr int kThreads = NT;
+  constexpr int kWarps = NT / 32;
   extern __shared__ __align__(16) unsigned char dyn_smem[];
-  __shared__ TileScratch<T, S> sc;
+  __shared__ TileScratch<T, S, kWarps> sc;
 
   const DevStructure& st = p.st;
   const SellView& sv = p.sell;
@@ -541,7 +547,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       const int q = tid;
       T stat = zero;
       int f = 1;
-#pragma unroll
+#pragma unroll 8
       for (int w = 0; w < kWarps; ++w) {
         stat = pmax(stat, sc.red[w][q][1]);
         f &= sc.redf[w][q];
@@ -618,7 +624,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       if (tid < S) {
         const int q = tid;
         T resb = zero, P = zero, Dp = zero, Rd = zero;
-#pragma unroll
+#pragma unroll 8
         for (int w = 0; w < kWarps; ++w) {
           resb = pmax(resb, sc.red[w][q][0]);
           P = P + sc.red[w][q][2];
@@ -670,7 +676,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       bool accepted = false;
       if (need_c) {  // need_c implies that phase B2 ran
         T res = sc.resb_it[q];
-#pragma unroll
+#pragma unroll 8
         for (int w = 0; w < kWarps; ++w) res = pmax(res, sc.red[w][q][5]);
         const T gap = sc.gap_it[q], stat = sc.stat_it[q];
         const T tol = sc.tol[q];
@@ -745,52 +751,64 @@ __global__ void arrange_values_kernel(const T* values, const int* slot, int coun
   }
 }
 
-template <typename T, int S, bool kShared>
+template <typename T, int S, int NT, bool kShared>
 cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaStream_t stream) {
   const unsigned grid = (unsigned)((p.batch + S - 1) / S);
   if (smem) {
-    auto kern = cp_forward_kernel<T, S, true, kShared>;
+    auto kern = cp_forward_kernel<T, S, NT, true, kShared>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem_bytes, stream>>>(p);
+    kern<<<grid, NT, smem_bytes, stream>>>(p);
   } else {
-    cp_forward_kernel<T, S, false, kShared><<<grid, kThreads, 0, stream>>>(p);
+    if constexpr (NT == kForwardThreads) {
+      cp_forward_kernel<T, S, NT, false, kShared><<<grid, NT, 0, stream>>>(p);
+    } else {
+      return cudaErrorInvalidValue;
+    }
   }
   return cudaGetLastError();
 }
 
+// Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads, and S = 1
+// with kWideThreads threads for shared-memory tiles of one sample.
 template <typename T, bool kShared>
-cudaError_t launch_shared(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
+cudaError_t launch_shared(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                           cudaStream_t stream) {
+  if (NT == kWideThreads)
+    return S == 1 ? launch_s<T, 1, kWideThreads, kShared>(p, smem, smem_bytes, stream)
+                  : cudaErrorInvalidValue;
+  if (NT != kForwardThreads) return cudaErrorInvalidValue;
   switch (S) {
-    case 1: return launch_s<T, 1, kShared>(p, smem, smem_bytes, stream);
-    case 2: return launch_s<T, 2, kShared>(p, smem, smem_bytes, stream);
-    case 4: return launch_s<T, 4, kShared>(p, smem, smem_bytes, stream);
-    case 8: return launch_s<T, 8, kShared>(p, smem, smem_bytes, stream);
+    case 1: return launch_s<T, 1, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
+    case 2: return launch_s<T, 2, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
+    case 4: return launch_s<T, 4, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
+    case 8: return launch_s<T, 8, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, int S, bool kShared>
+template <typename T, int S, int NT, bool kShared>
 int blocks_per_sm_s(size_t smem_bytes) {
-  auto kern = cp_forward_kernel<T, S, true, kShared>;
+  auto kern = cp_forward_kernel<T, S, NT, true, kShared>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes) !=
       cudaSuccess)
     return 0;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem_bytes) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem_bytes) != cudaSuccess)
     return 0;
   return per_sm;
 }
 
 template <typename T, bool kShared>
-int blocks_per_sm_shared(int S, size_t smem_bytes) {
+int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
+  if (NT == kWideThreads) return S == 1 ? blocks_per_sm_s<T, 1, kWideThreads, kShared>(smem_bytes) : 0;
+  if (NT != kForwardThreads) return 0;
   switch (S) {
-    case 1: return blocks_per_sm_s<T, 1, kShared>(smem_bytes);
-    case 2: return blocks_per_sm_s<T, 2, kShared>(smem_bytes);
-    case 4: return blocks_per_sm_s<T, 4, kShared>(smem_bytes);
-    case 8: return blocks_per_sm_s<T, 8, kShared>(smem_bytes);
+    case 1: return blocks_per_sm_s<T, 1, kForwardThreads, kShared>(smem_bytes);
+    case 2: return blocks_per_sm_s<T, 2, kForwardThreads, kShared>(smem_bytes);
+    case 4: return blocks_per_sm_s<T, 4, kForwardThreads, kShared>(smem_bytes);
+    case 8: return blocks_per_sm_s<T, 8, kForwardThreads, kShared>(smem_bytes);
     default: return 0;
   }
 }
@@ -798,18 +816,19 @@ int blocks_per_sm_shared(int S, size_t smem_bytes) {
 }  // namespace
 
 template <typename T>
-int forward_blocks_per_sm(int S, bool shared_values, size_t smem_bytes) {
-  return shared_values ? blocks_per_sm_shared<T, true>(S, smem_bytes)
-                       : blocks_per_sm_shared<T, false>(S, smem_bytes);
+int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes) {
+  return shared_values ? blocks_per_sm_shared<T, true>(S, NT, smem_bytes)
+                       : blocks_per_sm_shared<T, false>(S, NT, smem_bytes);
 }
 
 template <typename T>
-size_t forward_static_smem(int S) {
+size_t forward_static_smem(int S, int NT) {
+  if (NT == kWideThreads) return sizeof(TileScratch<T, 1, kWideThreads / 32>);
   switch (S) {
-    case 1: return sizeof(TileScratch<T, 1>);
-    case 2: return sizeof(TileScratch<T, 2>);
-    case 4: return sizeof(TileScratch<T, 4>);
-    default: return sizeof(TileScratch<T, 8>);
+    case 1: return sizeof(TileScratch<T, 1, kForwardThreads / 32>);
+    case 2: return sizeof(TileScratch<T, 2, kForwardThreads / 32>);
+    case 4: return sizeof(TileScratch<T, 4, kForwardThreads / 32>);
+    default: return sizeof(TileScratch<T, 8, kForwardThreads / 32>);
   }
 }
 
@@ -835,18 +854,20 @@ cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int 
 }
 
 template <typename T>
-cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
+cudaError_t launch_forward(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                            cudaStream_t stream) {
-  return p.vr ? launch_shared<T, true>(p, S, smem, smem_bytes, stream)
-              : launch_shared<T, false>(p, S, smem, smem_bytes, stream);
+  return p.vr ? launch_shared<T, true>(p, S, NT, smem, smem_bytes, stream)
+              : launch_shared<T, false>(p, S, NT, smem, smem_bytes, stream);
 }
 
-template cudaError_t launch_forward<double>(const FwdParams<double>&, int, bool, size_t, cudaStream_t);
-template cudaError_t launch_forward<float>(const FwdParams<float>&, int, bool, size_t, cudaStream_t);
-template int forward_blocks_per_sm<double>(int, bool, size_t);
-template int forward_blocks_per_sm<float>(int, bool, size_t);
-template size_t forward_static_smem<double>(int);
-template size_t forward_static_smem<float>(int);
+template cudaError_t launch_forward<double>(const FwdParams<double>&, int, int, bool, size_t,
+                                            cudaStream_t);
+template cudaError_t launch_forward<float>(const FwdParams<float>&, int, int, bool, size_t,
+                                           cudaStream_t);
+template int forward_blocks_per_sm<double>(int, int, bool, size_t);
+template int forward_blocks_per_sm<float>(int, int, bool, size_t);
+template size_t forward_static_smem<double>(int, int);
+template size_t forward_static_smem<float>(int, int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);
 template cudaError_t arrange_values<float>(const float*, const int*, int, float*, cudaStream_t);
 template cudaError_t permute_rows<double>(const double*, int64_t, const int*, int, int64_t, double*,

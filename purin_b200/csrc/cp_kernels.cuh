@@ -133,18 +133,23 @@ struct PostParams {
   uint8_t* elig;
 };
 
-// Threads per forward CTA.
+// Threads per forward CTA; kWideThreads for one-sample tiles whose state leaves
+// room for only one CTA of kForwardThreads per SM.
 constexpr int kForwardThreads = 256;
+constexpr int kWideThreads = 1024;
 
+// S samples per tile, NT threads per CTA; smem: the tile state lives in shared
+// memory (smem_bytes of it).
 template <typename T>
-cudaError_t launch_forward(const FwdParams<T>& p, int S, bool smem, size_t smem_bytes,
+cudaError_t launch_forward(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                            cudaStream_t stream);
+// Static shared memory of one forward CTA.
 template <typename T>
-size_t forward_static_smem(int S);
-// Resident CTAs per SM of the shared-memory forward kernel with S samples per tile
-// (0 when the occupancy query fails).
+size_t forward_static_smem(int S, int NT);
+// Resident CTAs per SM of the shared-memory forward kernel (0 when the
+// occupancy query fails).
 template <typename T>
-int forward_blocks_per_sm(int S, bool shared_values, size_t smem_bytes);
+int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
 // dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0 for b < rows.

@@ -62,7 +62,8 @@ struct PurinCpPlan {
   // Sliced-ELL layout (C = 32) in the internal row/column orders, built at creation.
   purin::SellView sell[1];
   void* sell_block = nullptr;
-  // Resident forward CTAs per SM by [diagonal steps][shared values][log2 S]
+  // Resident forward CTAs per SM by [diagonal steps][shared values][tile shape]
   // (-1: not queried yet); filled on first use, the same value by any thread.
-  int fwd_blocks[2][2][4] = {{{-1, -1, -1, -1}, {-1, -1, -1, -1}}, {{-1, -1, -1, -1}, {-1, -1, -1, -1}}};
+  int fwd_blocks[2][2][8] = {{{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
+                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}}};
 };

@@ -119,11 +119,15 @@ TILE_CASES = [
 _TILE_ORACLE = {}
 
 
-@pytest.mark.parametrize("samples_per_tile", [1, 2, 4, 8])
+@pytest.mark.parametrize("samples_per_tile,threads", [(1, 256), (2, 256), (4, 256), (8, 256),
+                                                     (1, 1024)])
 @pytest.mark.parametrize("name,dtype,overrides", TILE_CASES, ids=[c[0] for c in TILE_CASES])
-def test_forward_tile_widths_match_oracle(monkeypatch, samples_per_tile, name, dtype, overrides):
-    """Every tile width (samples per CTA), with a ragged last tile, gives the oracle's bits."""
+def test_forward_tile_widths_match_oracle(monkeypatch, samples_per_tile, threads, name, dtype,
+                                          overrides):
+    """Every tile shape (samples per CTA, threads per CTA), with a ragged last tile, gives the
+    oracle's bits."""
     monkeypatch.setenv("PURIN_CP_SAMPLES_PER_TILE", str(samples_per_tile))
+    monkeypatch.setenv("PURIN_CP_TILE_THREADS", str(threads))
     batch = 13
     w = make_workload(0, batch)
     cfg = replace(w.config, **overrides)
