@@ -102,19 +102,19 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
-  // fits, PURIN_CP_TILE_THREADS (256 or 1024) the threads per CTA.
+  // fits, PURIN_CP_TILE_THREADS (256, 512 or 1024) the threads per CTA.
   int forced = 0, forced_threads = 0;
   if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
   if (const char* env = std::getenv("PURIN_CP_TILE_THREADS")) forced_threads = std::atoi(env);
   // Default: the shape whose resident CTAs hold the most warps over the batch
   // (the iteration is latency-bound), then the most samples, then the first of
   // this list.  Every shape whose state fits in shared memory is a candidate.
-  static const int kShapes[5][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
+  static const int kShapes[6][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
                                     {4, purin::kForwardThreads}, {8, purin::kForwardThreads},
-                                    {1, purin::kWideThreads}};
+                                    {1, 2 * purin::kForwardThreads}, {1, purin::kWideThreads}};
   int best = -1;
   int64_t best_warps = -1, best_samples = -1;
-  for (int k = 0; k < 5; ++k) {
+  for (int k = 0; k < 6; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
     const size_t stat = f64 ? purin::forward_static_smem<double>(S, NT)
                             : purin::forward_static_smem<float>(S, NT);

@@ -207,10 +207,11 @@ __device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
   }
 }
 
-// Resident CTAs per SM the register budget is sized for: one 1024-thread CTA,
-// or 4 / 2 / 1 CTAs of 256 threads for S = 1 / 2 / wider.
+// Resident CTAs per SM the register budget is sized for (64 registers per
+// thread for one-sample tiles): 1 x 1024, 2 x 512, or 4 / 2 / 1 CTAs of 256
+// threads for S = 1 / 2 / wider.
 constexpr int forward_min_blocks(int S, int NT) {
-  return NT > kForwardThreads ? 1 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
+  return NT >= 1024 ? 1 : NT >= 512 ? 2 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
 }
 
 template <typename T, int S, int NT, bool kSmem, bool kShared>
@@ -771,10 +772,13 @@ cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaSt
 }
 
 // Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads, and S = 1
-// with kWideThreads threads for shared-memory tiles of one sample.
+// with 2 or 4 times as many threads for shared-memory tiles of one sample.
 template <typename T, bool kShared>
 cudaError_t launch_shared(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                           cudaStream_t stream) {
+  if (NT == 2 * kForwardThreads)
+    return S == 1 ? launch_s<T, 1, 2 * kForwardThreads, kShared>(p, smem, smem_bytes, stream)
+                  : cudaErrorInvalidValue;
   if (NT == kWideThreads)
     return S == 1 ? launch_s<T, 1, kWideThreads, kShared>(p, smem, smem_bytes, stream)
                   : cudaErrorInvalidValue;
@@ -802,6 +806,8 @@ int blocks_per_sm_s(size_t smem_bytes) {
 
 template <typename T, bool kShared>
 int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
+  if (NT == 2 * kForwardThreads)
+    return S == 1 ? blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared>(smem_bytes) : 0;
   if (NT == kWideThreads) return S == 1 ? blocks_per_sm_s<T, 1, kWideThreads, kShared>(smem_bytes) : 0;
   if (NT != kForwardThreads) return 0;
   switch (S) {
@@ -823,6 +829,7 @@ int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes) 
 
 template <typename T>
 size_t forward_static_smem(int S, int NT) {
+  if (NT == 2 * kForwardThreads) return sizeof(TileScratch<T, 1, 2 * kForwardThreads / 32>);
   if (NT == kWideThreads) return sizeof(TileScratch<T, 1, kWideThreads / 32>);
   switch (S) {
     case 1: return sizeof(TileScratch<T, 1, kForwardThreads / 32>);

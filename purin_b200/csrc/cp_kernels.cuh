@@ -133,8 +133,8 @@ struct PostParams {
   uint8_t* elig;
 };
 
-// Threads per forward CTA; kWideThreads for one-sample tiles whose state leaves
-// room for only one CTA of kForwardThreads per SM.
+// Threads per forward CTA; one-sample tiles whose state leaves room for only one
+// or two CTAs of kForwardThreads per SM run 2 x or 4 x (kWideThreads) as many.
 constexpr int kForwardThreads = 256;
 constexpr int kWideThreads = 1024;
 
