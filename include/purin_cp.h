@@ -19,6 +19,9 @@
  *                            restarted GMRES (primal_dual_interior_point/
  *                            operators.py:792-1125) on the CP fixed-point
  *                            adjoint, and the parameter pullback.
+ *   purin_cp_adjoint_stage <- the same backward one phase per call, so that
+ *                            shards of a batch can share the reference's
+ *                            batch-wide GMRES budget (operators.py:919-1103).
  *   purin_cp_postprocess  <- BoundProjection.solve post-processing
  *                            (bounds.py:247-317; solver.py:333-366): multiplier
  *                            recovery in original units, residuals, status.
@@ -76,6 +79,13 @@ typedef enum PurinCpIndex {
   PURIN_CP_KEPT_ROW_PTR = 5,    /* m_kept+1: CSR row pointer of the kept rows        */
   PURIN_CP_KEPT_COLS = 6        /* nnz_kept: column of each kept slot                */
 } PurinCpIndex;
+
+/* Phases of purin_cp_adjoint_stage. */
+typedef enum PurinCpStage {
+  PURIN_CP_STAGE_PREPARE = 0, /* step sizes, linearisation, initial residuals */
+  PURIN_CP_STAGE_CYCLE = 1,   /* one restarted-GMRES cycle                    */
+  PURIN_CP_STAGE_FINISH = 2   /* validity masking and parameter pullback      */
+} PurinCpStage;
 
 typedef struct PurinCpPlan PurinCpPlan;
 
@@ -228,6 +238,40 @@ int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config,
                          const PurinLinearSolverConfig* linear,
                          const PurinCpAdjointArgs* args, void* workspace,
                          size_t workspace_bytes, void* stream);
+
+/* purin_cp_adjoint_stage: purin_cp_adjoint one phase per call, for a batch
+ * split into shards (one per GPU, or chunks on one GPU) that must reproduce
+ * the unsharded batch exactly.  The reference solves the adjoint systems of
+ * the whole batch with one lockstep restarted GMRES
+ * (primal_dual_interior_point/operators.py:919-1103): every restart cycle
+ * lasts as many Arnoldi steps as the slowest active sample needs, and those
+ * steps are charged to ONE iteration budget (LinearSolverConfig.max_iterations)
+ * shared by the batch.  A shard that ran its own loop would charge only its
+ * own cycles and could give a sample a longer final cycle than the full batch
+ * would.  The staged form exposes the two numbers the shards must agree on:
+ *
+ *   PREPARE  (completed ignored)  counters <- {0, samples above threshold}
+ *   CYCLE    (completed = Arnoldi steps taken so far by the whole batch, in
+ *             [0, max_iterations))  counters <- {steps of this cycle (max
+ *             over the shard's samples), samples still above threshold}
+ *   FINISH   (counters may be NULL)  writes the outputs of purin_cp_adjoint.
+ *
+ * The driver (every shard identically): PREPARE; combine the counters of all
+ * shards by elementwise MAX (e.g. an NCCL all-reduce on the counters' device
+ * words); completed = 0; while completed < max_iterations and combined[1] > 0:
+ * CYCLE(completed), combine, completed += combined[0]; then FINISH.  With the
+ * combined counters every shard's results equal the unsharded purin_cp_adjoint's
+ * bit for bit; with one shard they equal purin_cp_adjoint's output.
+ * `counters` is a device array of two int32; args, workspace and stream must
+ * be the same for all phases of one solve (the workspace carries the state).
+ * An empty shard (batch 0) still reports zero counters.  The phases are
+ * ordinary (non-cooperative) launches on `stream` and do not synchronise; the
+ * driver does, when it reads the combined counters on the host. */
+int32_t purin_cp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* config,
+                               const PurinLinearSolverConfig* linear,
+                               const PurinCpAdjointArgs* args, int32_t stage,
+                               int32_t completed, int32_t* counters, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args,
                              void* stream);

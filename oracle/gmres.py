@@ -28,24 +28,51 @@ def _hypot(x, y):
     return np.where(inf, dtype.type(np.inf), r)
 
 
-def batched_restarted_gmres(matvec, rhs, *, tolerance, absolute_tolerance, restart,
-                            max_iterations, stats=None):
-    """Solve matvec(x) = rhs per row; returns (x, info, residual_inf)."""
-    batch, width = rhs.shape
-    dtype = rhs.dtype
-    restart = int(min(restart, max_iterations, width))
-    eps = dtype.type(1e-30)
-    breakdown = dtype.type(1e-14)
-    zero = dtype.type(0)
-    rhs_scale = np.max(np.abs(rhs), axis=1, initial=0.0).astype(dtype)
-    threshold = np.maximum(dtype.type(absolute_tolerance), dtype.type(tolerance) * rhs_scale)
+class LockstepGmres:
+    """The batched restarted GMRES of ``operators.py:792-1125``, one cycle per call.
 
-    x = np.zeros_like(rhs)
-    residual_inf = np.max(np.abs(rhs - matvec(x)), axis=1, initial=0.0).astype(dtype)
-    completed = 0
-    cycles = 0
-    while completed < max_iterations and np.any(residual_inf > threshold):
-        cycle_limit = min(restart, max_iterations - completed)
+    ``prepare`` computes the thresholds and initial residuals; ``cycle(completed)``
+    runs one restart cycle (``cycle_body``, operators.py:919-1097) with the
+    budget ``min(restart, max_iterations - completed)`` and returns this batch's
+    counters (the cycle's Arnoldi steps, samples still above threshold);
+    ``result`` gives ``(x, info, residual_inf)`` (operators.py:1109-1125).  Run
+    back to back over the whole batch (``batched_restarted_gmres``) this is the
+    reference's loop; run per shard with the shards' counters combined by max
+    it is the same loop split across shards.
+    """
+
+    def __init__(self, matvec, rhs, *, tolerance, absolute_tolerance, restart, max_iterations):
+        self.matvec = matvec
+        self.rhs = rhs
+        batch, width = rhs.shape
+        dtype = rhs.dtype
+        self.dtype = dtype
+        self.max_iterations = int(max_iterations)
+        self.restart = int(min(restart, max_iterations, width))
+        rhs_scale = np.max(np.abs(rhs), axis=1, initial=0.0).astype(dtype)
+        self.threshold = np.maximum(dtype.type(absolute_tolerance),
+                                    dtype.type(tolerance) * rhs_scale)
+        self.x = None
+        self.residual_inf = None
+
+    def prepare(self):
+        rhs = self.rhs
+        self.x = np.zeros_like(rhs)
+        self.residual_inf = np.max(np.abs(rhs - self.matvec(self.x)), axis=1,
+                                   initial=0.0).astype(self.dtype)
+        return 0, int(np.sum(self.residual_inf > self.threshold))
+
+    def cycle(self, completed):
+        matvec, rhs, x = self.matvec, self.rhs, self.x
+        batch, width = rhs.shape
+        dtype = self.dtype
+        restart = self.restart
+        threshold = self.threshold
+        residual_inf = self.residual_inf
+        eps = dtype.type(1e-30)
+        breakdown = dtype.type(1e-14)
+        zero = dtype.type(0)
+        cycle_limit = min(restart, self.max_iterations - completed)
         residual = rhs - matvec(x)
         beta = np.sqrt(np.sum(residual * residual, axis=1))
         safe_beta = np.maximum(beta, eps)
@@ -119,10 +146,30 @@ def batched_restarted_gmres(matvec, rhs, *, tolerance, absolute_tolerance, resta
         cand_res = np.max(np.abs(rhs - matvec(candidate)), axis=1, initial=0.0).astype(dtype)
         x = np.where(cycle_active[:, None], candidate, x)
         residual_inf = np.where(cycle_active, cand_res, residual_inf)
-        completed += it
+        self.x = x
+        self.residual_inf = residual_inf
+        return it, int(np.sum(residual_inf > threshold))
+
+    def result(self):
+        x, residual_inf = self.x, self.residual_inf
+        finite = np.all(np.isfinite(x), axis=1) & np.isfinite(residual_inf)
+        info = np.where(~finite, 2, np.where(residual_inf <= self.threshold, 0, 1)).astype(np.int32)
+        return x, info, residual_inf
+
+
+def batched_restarted_gmres(matvec, rhs, *, tolerance, absolute_tolerance, restart,
+                            max_iterations, stats=None):
+    """Solve matvec(x) = rhs per row; returns (x, info, residual_inf)."""
+    solver = LockstepGmres(matvec, rhs, tolerance=tolerance,
+                           absolute_tolerance=absolute_tolerance, restart=restart,
+                           max_iterations=max_iterations)
+    _, active = solver.prepare()
+    completed = 0
+    cycles = 0
+    while completed < max_iterations and active > 0:
+        steps, active = solver.cycle(completed)
+        completed += steps
         cycles += 1
-    finite = np.all(np.isfinite(x), axis=1) & np.isfinite(residual_inf)
-    info = np.where(~finite, 2, np.where(residual_inf <= threshold, 0, 1)).astype(np.int32)
     if stats is not None:
         stats.update(completed=completed, cycles=cycles)
-    return x, info, residual_inf
+    return solver.result()

@@ -31,7 +31,7 @@ from oracle.cp import (
     operators,
     sparse_cp,
 )
-from oracle.gmres import batched_restarted_gmres
+from oracle.gmres import LockstepGmres, batched_restarted_gmres
 from oracle.sparse import layout
 
 CONVERGED, MAX_ITERATIONS, LINEAR_SOLVE_FAILURE, NONFINITE = 0, 1, 2, 3
@@ -233,9 +233,8 @@ class OracleProjection:
                                 saved["target"], saved["lower"], saved["upper"],
                                 self.support, self.mask, self.me, tau, sigma, (v_y, v_d, v_b))
 
-    def vjp(self, saved, cot_y, stats=None):
-        """``bounds.py:80-165``: GMRES on (I - J^T) v = g, then the parameter pullback."""
-        cfg = self.config
+    def _vjp_system(self, saved, cot_y):
+        """Step sizes, the operator I - J^T and the right-hand side g (``bounds.py:83-138``)."""
         out = saved["out"]
         target = saved["target"]
         dtype = target.dtype
@@ -249,16 +248,61 @@ class OracleProjection:
 
         g = np.concatenate((np.where(out.converged[:, None], cot_y, zero),
                             np.zeros_like(out.dual), np.zeros_like(out.y)), axis=1)
-        adjoint, code, residual = batched_restarted_gmres(
-            operator, g, tolerance=cfg.linear_tolerance,
-            absolute_tolerance=cfg.linear_atol, restart=cfg.linear_restart,
-            max_iterations=cfg.linear_max_iterations, stats=stats)
+        return tau, sigma, operator, g
+
+    def _vjp_gradients(self, saved, tau, sigma, adjoint, code, residual):
+        """Validity masking and the parameter pullback (``bounds.py:148-165``)."""
+        cfg = self.config
+        out = saved["out"]
+        dtype = saved["target"].dtype
+        zero = dtype.type(0)
         valid = (out.converged & np.all(np.isfinite(adjoint), axis=1) & np.isfinite(residual)
                  & ((code == 0) | (residual <= dtype.type(cfg.adjoint_tolerance))))
         adjoint = np.where(valid[:, None], adjoint, zero)
         _, gv, gb, gt, gl, gu = self.pullback(saved, tau, sigma, adjoint)
         clean = lambda a: np.nan_to_num(a, nan=0.0, posinf=0.0, neginf=0.0)
+        grads = dict(values=clean(gv), rhs=clean(gb), target=clean(gt), lower=clean(gl),
+                     upper=clean(gu))
+        return grads, valid
+
+    def vjp(self, saved, cot_y, stats=None):
+        """``bounds.py:80-165``: GMRES on (I - J^T) v = g, then the parameter pullback."""
+        cfg = self.config
+        tau, sigma, operator, g = self._vjp_system(saved, cot_y)
+        adjoint, code, residual = batched_restarted_gmres(
+            operator, g, tolerance=cfg.linear_tolerance,
+            absolute_tolerance=cfg.linear_atol, restart=cfg.linear_restart,
+            max_iterations=cfg.linear_max_iterations, stats=stats)
+        grads, valid = self._vjp_gradients(saved, tau, sigma, adjoint, code, residual)
         if stats is not None:
             stats.update(code=code, residual=residual, valid=valid, tau=tau, sigma=sigma)
-        return dict(values=clean(gv), rhs=clean(gb), target=clean(gt), lower=clean(gl),
-                    upper=clean(gu))
+        return grads
+
+    def vjp_shard(self, saved, cot_y):
+        """The VJP of one shard of a batch, in the phases a lockstep driver combines.
+
+        ``prepare()`` and ``cycle(completed)`` return this shard's GMRES counters;
+        ``finish()`` returns ``(gradients, code, residual)``.  Driven with the
+        counters of all shards combined by max, the shards reproduce ``vjp`` of
+        the whole batch (one batch-wide budget, ``operators.py:919-1103``).
+        """
+        cfg = self.config
+        tau, sigma, operator, g = self._vjp_system(saved, cot_y)
+        solver = LockstepGmres(operator, g, tolerance=cfg.linear_tolerance,
+                               absolute_tolerance=cfg.linear_atol, restart=cfg.linear_restart,
+                               max_iterations=cfg.linear_max_iterations)
+        projection = self
+
+        class _Shard:
+            def prepare(self):
+                return solver.prepare()
+
+            def cycle(self, completed):
+                return solver.cycle(completed)
+
+            def finish(self):
+                adjoint, code, residual = solver.result()
+                grads, _ = projection._vjp_gradients(saved, tau, sigma, adjoint, code, residual)
+                return grads, code, residual
+
+        return _Shard()

@@ -17,6 +17,7 @@ ABI_VERSION = 1
 
 PURIN_FLOAT64, PURIN_FLOAT32 = 0, 1
 OP_FORWARD, OP_ADJOINT = 0, 1
+STAGE_PREPARE, STAGE_CYCLE, STAGE_FINISH = 0, 1, 2
 KEPT_ROWS, KEPT_SLOTS, BOUND_ROWS, BOUND_SLOTS, BOUND_VARIABLES, KEPT_ROW_PTR, KEPT_COLS = range(7)
 
 c_i32, c_i64, c_dbl, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_double, ctypes.c_void_p
@@ -77,7 +78,8 @@ class PostArgs(ctypes.Structure):
 EXPORTED = (
     "purin_cp_abi_version", "purin_cp_last_error", "purin_cp_plan_create",
     "purin_cp_plan_destroy", "purin_cp_plan_info", "purin_cp_plan_indices",
-    "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_postprocess",
+    "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_adjoint_stage",
+    "purin_cp_postprocess",
 )
 
 _lib = None
@@ -113,10 +115,14 @@ def load():
                                      c_vp, ctypes.c_size_t, c_vp]
     lib.purin_cp_adjoint.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(LinearConfig),
                                      ctypes.POINTER(AdjointArgs), c_vp, ctypes.c_size_t, c_vp]
+    lib.purin_cp_adjoint_stage.argtypes = [c_vp, ctypes.POINTER(CpConfig),
+                                           ctypes.POINTER(LinearConfig),
+                                           ctypes.POINTER(AdjointArgs), c_i32, c_i32, c_vp, c_vp,
+                                           ctypes.c_size_t, c_vp]
     lib.purin_cp_postprocess.argtypes = [c_vp, ctypes.POINTER(PostArgs), c_vp]
     for name in ("purin_cp_plan_create", "purin_cp_plan_destroy", "purin_cp_plan_info",
                  "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward",
-                 "purin_cp_adjoint", "purin_cp_postprocess"):
+                 "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess"):
         getattr(lib, name).restype = c_i32
     version = lib.purin_cp_abi_version()
     if version != ABI_VERSION:
@@ -179,6 +185,13 @@ class Plan:
         check(self._lib.purin_cp_adjoint(self.handle, ctypes.byref(cfg), ctypes.byref(lin),
                                          ctypes.byref(args), workspace_ptr, workspace_bytes,
                                          stream), "purin_cp_adjoint")
+
+    def adjoint_stage(self, cfg, lin, args, stage, completed, counters_ptr, workspace_ptr,
+                      workspace_bytes, stream):
+        check(self._lib.purin_cp_adjoint_stage(self.handle, ctypes.byref(cfg), ctypes.byref(lin),
+                                               ctypes.byref(args), stage, completed, counters_ptr,
+                                               workspace_ptr, workspace_bytes, stream),
+              "purin_cp_adjoint_stage")
 
     def postprocess(self, args, stream):
         check(self._lib.purin_cp_postprocess(self.handle, ctypes.byref(args), stream),

@@ -320,19 +320,9 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
 }
 
 template <typename T>
-int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
-                    const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
-                    cudaStream_t stream) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
-  if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
-  if (workspace == nullptr || workspace_bytes < L.total)
-    return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
-  if (!a->device_error) return fail(PURIN_ERR_INVALID_ARGUMENT, "device_error pointer is required");
-  char* ws = static_cast<char*>(workspace);
-  cudaError_t e = cudaMemsetAsync(ws + L.off_counters, 0, L.counters_bytes, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
-  e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
-  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
+purin::AdjParams<T> adjoint_params(const PurinCpPlan* plan, const PurinCpConfig* cfg,
+                                   const PurinLinearSolverConfig* lin, const PurinCpAdjointArgs* a,
+                                   const AdjLayout& L, char* ws) {
   purin::AdjParams<T> p{};
   p.st = plan->dev;
   p.batch = a->batch;
@@ -383,8 +373,74 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.cycle_len = counters;
   p.cycle_act = counters + (lin->max_iterations + 2);
   p.barrier = reinterpret_cast<purin::GridBarrier*>(counters + 2 * (lin->max_iterations + 2));
+  p.stage = 0;
+  p.completed0 = 0;
+  return p;
+}
+
+template <typename T>
+int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
+                    const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
+  if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
+  if (!a->device_error) return fail(PURIN_ERR_INVALID_ARGUMENT, "device_error pointer is required");
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaMemsetAsync(ws + L.off_counters, 0, L.counters_bytes, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
+  e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
+  const purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
   e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch");
+  return PURIN_OK;
+}
+
+// One phase of the adjoint (see purin_cp_adjoint_stage in the header).  The
+// counters of the phase go to the caller's two words: stage PREPARE writes
+// {0, samples above their GMRES threshold}; stage CYCLE writes {Arnoldi steps
+// of the cycle (the largest over this shard's samples), samples still above
+// their threshold after it}.
+template <typename T>
+int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
+                          const PurinCpAdjointArgs* a, int32_t stage, int32_t completed, int32_t* counters,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
+  if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
+  if (!a->device_error) return fail(PURIN_ERR_INVALID_ARGUMENT, "device_error pointer is required");
+  char* ws = static_cast<char*>(workspace);
+  cudaError_t e = cudaSuccess;
+  if (stage == PURIN_CP_STAGE_PREPARE) {
+    e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage memset");
+  }
+  if (stage != PURIN_CP_STAGE_FINISH) {
+    e = cudaMemsetAsync(counters, 0, 2 * sizeof(int32_t), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage memset");
+  }
+  purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
+  unsigned* words = reinterpret_cast<unsigned*>(counters);
+  p.barrier = nullptr;
+  p.completed0 = completed;
+  if (stage == PURIN_CP_STAGE_PREPARE) {
+    p.stage = 1;
+    p.cycle_len = words;      // unused by the prepare phase
+    p.cycle_act = words + 1;  // cycle_act[0] -> word 1
+  } else if (stage == PURIN_CP_STAGE_CYCLE) {
+    p.stage = 2;
+    p.cycle_len = words;  // cycle_len[0] -> word 0
+    p.cycle_act = words;  // cycle_act[1] -> word 1
+  } else {
+    p.stage = 3;
+    p.cycle_len = nullptr;
+    p.cycle_act = nullptr;
+  }
+  e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage launch");
   return PURIN_OK;
 }
 
@@ -490,6 +546,17 @@ void build_csc(int n, const std::vector<int32_t>& row_ptr, const std::vector<int
   }
 }
 
+int32_t check_adjoint_args(const PurinCpPlan* plan, const PurinCpAdjointArgs* args) {
+  const int m = plan->info.kept_rows;
+  if (!args->target || !args->lower || !args->upper || !args->y || !args->converged || !args->cot_y ||
+      (m > 0 && (!args->rhs || !args->dual)) || (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required adjoint array is NULL");
+  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or kept_nnz");
+  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  return PURIN_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -817,6 +884,39 @@ int32_t purin_cp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, c
                                            : run_forward<float>(plan, config, args, workspace, workspace_bytes, s);
 }
 
+
+int32_t purin_cp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* config,
+                               const PurinLinearSolverConfig* linear, const PurinCpAdjointArgs* args,
+                               int32_t stage, int32_t completed, int32_t* counters, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (stage != PURIN_CP_STAGE_PREPARE && stage != PURIN_CP_STAGE_CYCLE && stage != PURIN_CP_STAGE_FINISH)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown adjoint stage");
+  if (stage != PURIN_CP_STAGE_FINISH && !counters)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "counters is NULL");
+  if (stage == PURIN_CP_STAGE_CYCLE && (completed < 0 || completed >= linear->max_iterations))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "completed must lie in [0, max_iterations) for a cycle");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (args->batch == 0) {
+    // An empty shard still takes part in the exchange: it reports zeros.
+    if (stage == PURIN_CP_STAGE_FINISH) return PURIN_OK;
+    cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(int32_t), s);
+    return e == cudaSuccess ? PURIN_OK : cuda_fail(e, "purin_cp_adjoint_stage memset");
+  }
+  if (int32_t r = check_adjoint_args(plan, args)) return r;
+  return plan->info.dtype == PURIN_FLOAT64
+             ? run_adjoint_stage<double>(plan, config, linear, args, stage, completed, counters, workspace,
+                                         workspace_bytes, s)
+             : run_adjoint_stage<float>(plan, config, linear, args, stage, completed, counters, workspace,
+                                        workspace_bytes, s);
+}
+
 int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
                          const PurinCpAdjointArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
   if (int32_t r = check_plan(plan)) return r;
@@ -825,14 +925,7 @@ int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, c
   if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
   if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
   if (args->batch == 0) return PURIN_OK;
-  const int m = plan->info.kept_rows;
-  if (!args->target || !args->lower || !args->upper || !args->y || !args->converged || !args->cot_y ||
-      (m > 0 && (!args->rhs || !args->dual)) || (plan->info.kept_nnz > 0 && !args->values))
-    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required adjoint array is NULL");
-  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
-    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or kept_nnz");
-  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
-    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  if (int32_t r = check_adjoint_args(plan, args)) return r;
   DeviceGuard guard(plan->info.device);
   if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

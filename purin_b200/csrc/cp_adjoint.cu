@@ -22,6 +22,14 @@
 // length (the largest number of Arnoldi steps any sample took) and the count
 // of samples still above their threshold, which set the shared iteration
 // budget and the loop condition (operators.py:919-1103).
+//
+// Staged mode runs the same code one phase per launch (p.stage 1: step sizes,
+// linearisation and initial residuals; 2: one GMRES cycle; 3: validity and
+// pullback) and reports the cycle's counters in two words, so that a host
+// holding one shard of a batch can combine them with the other shards' (an
+// elementwise max) before the next cycle: the shards then share the
+// reference's batch-wide budget exactly.  State between launches lives in the
+// workspace (x, thresholds, residuals, linearisation codes).
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -274,13 +282,14 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
   const T zero = T(0), one = T(1);
   const T eps = T(1e-30), breakdown = T(1e-14);
   const unsigned nblocks = gridDim.x;
+  const int stage = p.stage;
 
   // ---- phase 0: step sizes, linearisation, right-hand side ----------------
   // A sample whose forward solve did not converge has right-hand side
   // g = (where(converged, cot, 0), 0, 0) = 0 (bounds.py:133), so x = 0 solves its
   // system exactly and its gradients are zeros (bounds.py:148-165): it is not
   // linearised, never enters GMRES and gets zeros in the final phase.
-  for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+  for (int64_t X = blockIdx.x; stage <= 1 && X < p.batch; X += gridDim.x) {
     if (p.converged[X] == 0) {
       if (threadIdx.x == 0) {
         p.thresh[X] = pmax(p.lin_atol, zero);
@@ -399,15 +408,18 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     __syncthreads();
   }
 
-  if (!grid_barrier(p.barrier, nblocks, p.timeout_ns)) {
+  if (stage == 1) return;
+  if (stage == 0 && !grid_barrier(p.barrier, nblocks, p.timeout_ns)) {
     if (threadIdx.x == 0) atomicExch(p.device_error, 1);
     return;
   }
 
   // ---- GMRES cycles in lockstep over the batch ------------------------------
-  int completed = 0;
+  // Staged: exactly one cycle, whose budget and loop condition the host has
+  // already established from the combined counters of every shard.
+  int completed = stage == 2 ? p.completed0 : 0;
   int cycle = 0;
-  bool any = atomicOr(&p.cycle_act[0], 0u) > 0;
+  bool any = stage == 2 ? true : (stage == 0 && atomicOr(&p.cycle_act[0], 0u) > 0);
   while (completed < p.max_it && any) {
     const int limit = min(R, p.max_it - completed);
     for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
@@ -525,6 +537,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       }
       __syncthreads();
     }
+    if (stage == 2) return;
     if (!grid_barrier(p.barrier, nblocks, p.timeout_ns)) {
       if (threadIdx.x == 0) atomicExch(p.device_error, 1);
       return;
@@ -535,7 +548,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
   }
 
   // ---- validity and parameter pullback (bounds.py:148-165) ------------------
-  for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
+  for (int64_t X = blockIdx.x; (stage == 0 || stage == 3) && X < p.batch; X += gridDim.x) {
     if (p.converged[X] == 0) {
       // Zero right-hand side: zero solution (status 0, residual 0), zero gradients.
       for (int j = threadIdx.x; j < n; j += kThreads) {
@@ -655,16 +668,13 @@ cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors, c
   const int n = p.st.n, m = p.st.m;
   const size_t smem = adjoint_smem_bytes<T>(n, m, p.R, smem_vectors);
   void* args[] = {(void*)&p};
-  if (smem_vectors) {
-    auto kern = cp_adjoint_kernel<T, true>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
-  }
-  auto kern = cp_adjoint_kernel<T, false>;
+  auto kern = smem_vectors ? cp_adjoint_kernel<T, true> : cp_adjoint_kernel<T, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
+  // Only the fused launch has grid barriers, so only it needs co-residency.
+  if (p.stage == 0)
+    return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
+  return cudaLaunchKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
 }
 
 template size_t adjoint_smem_bytes<double>(int, int, int, bool);

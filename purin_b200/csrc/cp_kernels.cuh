@@ -91,6 +91,11 @@ struct AdjParams {
   int R;       // effective restart = min(restart, max_iterations, W)
   int max_it;  // GMRES iteration budget
   uint64_t timeout_ns;
+  // 0: the whole VJP in one cooperative launch (grid barriers between phases).
+  // 1, 2, 3: one phase per launch (prepare; one GMRES cycle; pullback) for a
+  // host that exchanges the cycle counters with other shards between launches.
+  int stage;
+  int completed0;  // stage 2: Arnoldi steps the lockstep batch has taken so far
   // workspace
   T* x;            // B * W
   T* lamp;         // B * m

@@ -23,7 +23,7 @@ from typing import NamedTuple
 import numpy as np
 import torch
 
-from purin_b200 import _native
+from purin_b200 import _native, lockstep
 from purin_b200.config import ChambollePockConfig
 from purin_b200.problems import CanonicalAffine, canonical_of, ell_index, rows_of
 from purin_b200.types import (
@@ -193,6 +193,7 @@ class PreparedChambollePockProjection:
         set_("_constant", None)
         set_("_sample_offset", 0)
         set_("_total_batch", int(self.batch_size))
+        set_("_lockstep_group", None)
         set_("_timers", None)
 
     # -- sizes -----------------------------------------------------------------
@@ -212,16 +213,24 @@ class PreparedChambollePockProjection:
     def inequality_size(self):
         return int(self.canonical.inequality_size)
 
-    def set_shard(self, offset: int, total: int):
+    def set_shard(self, offset: int, total: int, group=None):
         """Declare this layer's batch as rows ``offset..`` of a global batch of ``total``.
 
-        Only the seeded power iteration depends on a sample's global index (its
-        PRNG key is ``split(PRNGKey(seed), total)[offset + b]``); sharding the
-        batch across devices with the right offsets reproduces the unsharded
-        results exactly.
+        Two things couple a sample to the rest of the batch in the reference.
+        The seeded power iteration draws sample ``b``'s start vector from
+        ``split(PRNGKey(seed), total)[offset + b]``, which the offset fixes.  And
+        the adjoint's restarted GMRES charges one iteration budget for the whole
+        batch (operators.py:919-1103): given ``group`` (a ``torch.distributed``
+        process group whose ranks hold the other shards, each calling
+        ``set_shard`` with the same group), the backward runs in phases and
+        all-reduces the two GMRES counters across the group after each one, so
+        the gradients equal the unsharded batch's in every case.  Without a group
+        each shard keeps its own budget, which gives the same gradients unless a
+        sample needs more restart cycles than the budget allows the batch.
         """
         object.__setattr__(self, "_sample_offset", int(offset))
         object.__setattr__(self, "_total_batch", int(total))
+        object.__setattr__(self, "_lockstep_group", group)
 
     # -- native calls --------------------------------------------------------------
     def _stream(self):
@@ -265,31 +274,21 @@ class PreparedChambollePockProjection:
 
     def _adjoint_native(self, data, rhs, target, lower, upper, y, dual, converged, gy, *,
                         need_values, need_rhs, need_target, need_lower, need_upper):
-        batch, n = target.shape
-        m = self._m
-        dev, dt = self._device, target.dtype
-        g_values = torch.empty((batch, data.shape[1]), dtype=dt, device=dev) if need_values else None
-        g_rhs = torch.empty((batch, m), dtype=dt, device=dev) if need_rhs else None
-        g_target = torch.empty((batch, n), dtype=dt, device=dev) if need_target else None
-        g_lower = torch.empty((batch, n), dtype=dt, device=dev) if need_lower else None
-        g_upper = torch.empty((batch, n), dtype=dt, device=dev) if need_upper else None
-        status = torch.empty((batch,), dtype=torch.int32, device=dev)
-        lres = torch.empty((batch,), dtype=dt, device=dev)
-        err = torch.zeros((1,), dtype=torch.int32, device=dev)
-        ws_bytes = self._plan.workspace_size(_native.OP_ADJOINT, batch, self._cfg, self._lin)
-        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
-        args = _native.AdjointArgs(
-            batch, _ptr(data), 0 if data.shape[0] == 1 and batch != 1 else data.shape[1],
-            _ptr(rhs), _ptr(target), _ptr(lower), _ptr(upper),
-            0 if lower.shape[0] == 1 and batch != 1 else n, _ptr(y), _ptr(dual), _ptr(converged),
-            _ptr(gy), self._sample_offset, self._total_batch, _ptr(g_values), _ptr(g_rhs),
-            _ptr(g_target), _ptr(g_lower), _ptr(g_upper), _ptr(status), _ptr(lres), _ptr(err))
-        with self._timed("adjoint"):
-            self._plan.adjoint(self._cfg, self._lin, args, ws.data_ptr(), ws_bytes, self._stream())
-        object.__setattr__(self, "_last_linear", (status, lres))
-        if int(err.item()) != 0:
-            raise RuntimeError("purin_cp_adjoint: a bounded device wait timed out; gradients are invalid")
-        return g_values, g_rhs, g_target, g_lower, g_upper
+        shard = self._adjoint_shard(data, rhs, target, lower, upper, y, dual, converged, gy,
+                                    need_values=need_values, need_rhs=need_rhs,
+                                    need_target=need_target, need_lower=need_lower,
+                                    need_upper=need_upper)
+        if self._lockstep_group is None:
+            return shard.fused()
+        (grads,), _, _ = lockstep.run([shard], int(self._lin.max_iterations),
+                                      group=self._lockstep_group)
+        return grads
+
+    def _adjoint_shard(self, data, rhs, target, lower, upper, y, dual, converged, gy, *,
+                       need_values, need_rhs, need_target, need_lower, need_upper):
+        """The backward of this layer's batch as a shard of ``purin_b200.lockstep``."""
+        return _AdjointShard(self, data, rhs, target, lower, upper, y, dual, converged, gy,
+                             (need_values, need_rhs, need_target, need_lower, need_upper))
 
     # -- preprocessing -----------------------------------------------------------------
     def _row_scale(self, kept):
@@ -437,6 +436,79 @@ class PreparedChambollePockProjection:
         if self._n_bound == 0:
             return None
         return SimpleNamespace(rows=self._kept_rows.tolist(), bound_rows=self._bound_rows.tolist())
+
+
+class _AdjointShard:
+    """Outputs, workspace and C-ABI arguments of one adjoint call.
+
+    ``fused()`` runs the whole VJP in one launch (``purin_cp_adjoint``);
+    ``prepare``/``cycle``/``finish`` run it in phases (``purin_cp_adjoint_stage``)
+    for ``purin_b200.lockstep.run``, returning the shard's GMRES counters as a
+    two-element device tensor.
+    """
+
+    def __init__(self, layer, data, rhs, target, lower, upper, y, dual, converged, gy, need):
+        batch, n = target.shape
+        m = layer._m
+        dev, dt = layer._device, target.dtype
+        need_values, need_rhs, need_target, need_lower, need_upper = need
+        empty = lambda shape, dtype=dt: torch.empty(shape, dtype=dtype, device=dev)
+        self.layer = layer
+        self.grads = (empty((batch, data.shape[1])) if need_values else None,
+                      empty((batch, m)) if need_rhs else None,
+                      empty((batch, n)) if need_target else None,
+                      empty((batch, n)) if need_lower else None,
+                      empty((batch, n)) if need_upper else None)
+        self.status = empty((batch,), torch.int32)
+        self.lres = empty((batch,))
+        self.err = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.counters = torch.zeros((2,), dtype=torch.int32, device=dev)
+        self.ws_bytes = layer._plan.workspace_size(_native.OP_ADJOINT, batch, layer._cfg,
+                                                   layer._lin)
+        self.ws = torch.empty((max(self.ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        g_values, g_rhs, g_target, g_lower, g_upper = self.grads
+        self.args = _native.AdjointArgs(
+            batch, _ptr(data), 0 if data.shape[0] == 1 and batch != 1 else data.shape[1],
+            _ptr(rhs), _ptr(target), _ptr(lower), _ptr(upper),
+            0 if lower.shape[0] == 1 and batch != 1 else n, _ptr(y), _ptr(dual), _ptr(converged),
+            _ptr(gy), layer._sample_offset, layer._total_batch, _ptr(g_values), _ptr(g_rhs),
+            _ptr(g_target), _ptr(g_lower), _ptr(g_upper), _ptr(self.status), _ptr(self.lres),
+            _ptr(self.err))
+        # Keep every buffer the arguments point at alive for the shard's lifetime.
+        self._inputs = (data, rhs, target, lower, upper, y, dual, converged, gy)
+
+    def _done(self):
+        layer = self.layer
+        object.__setattr__(layer, "_last_linear", (self.status, self.lres))
+        if int(self.err.item()) != 0:
+            raise RuntimeError("purin_cp_adjoint: a bounded device wait timed out; "
+                               "gradients are invalid")
+        return self.grads
+
+    def fused(self):
+        layer = self.layer
+        with layer._timed("adjoint"):
+            layer._plan.adjoint(layer._cfg, layer._lin, self.args, self.ws.data_ptr(),
+                                self.ws_bytes, layer._stream())
+        return self._done()
+
+    def _stage(self, stage, completed=0):
+        layer = self.layer
+        with layer._timed("adjoint"):
+            layer._plan.adjoint_stage(layer._cfg, layer._lin, self.args, stage, completed,
+                                      self.counters.data_ptr(), self.ws.data_ptr(),
+                                      self.ws_bytes, layer._stream())
+        return self.counters
+
+    def prepare(self):
+        return self._stage(_native.STAGE_PREPARE)
+
+    def cycle(self, completed):
+        return self._stage(_native.STAGE_CYCLE, completed)
+
+    def finish(self):
+        self._stage(_native.STAGE_FINISH)
+        return self._done()
 
 
 def _ndim(x):

@@ -1,0 +1,79 @@
+"""Batch-wide lockstep of the adjoint's restarted GMRES across shards of a batch.
+
+The reference solves the implicit-differentiation systems of a whole batch
+with ONE lockstep restarted GMRES (``_batched_restarted_gmres``,
+``src/purin/solvers/primal_dual_interior_point/operators.py:919-1103``):
+
+* a restart cycle runs Arnoldi steps while ANY sample of the batch is still
+  active (``arnoldi_condition``, operators.py:943-955), so the cycle lasts as
+  many steps as its slowest sample needs;
+* those steps are charged to one budget, ``completed_iterations``
+  (operators.py:1093), and the next cycle may take at most
+  ``min(restart, max_iterations - completed_iterations)`` steps
+  (operators.py:921-924);
+* cycles continue while any sample's true residual is above its threshold
+  (``cycle_condition``, operators.py:1099-1103).
+
+When the batch is split into shards (one per GPU, or chunks on one GPU) each
+shard must therefore learn, after every cycle, the longest cycle and whether
+any sample anywhere is still active; otherwise a shard whose own samples
+finish their cycles early is left a larger budget and can run a longer final
+cycle than the unsharded batch would.  ``run`` drives shards through the
+staged adjoint (``purin_cp_adjoint_stage``): it combines their two counters
+with an elementwise max, locally over the shards of this process and, given a
+process group, across ranks with one all-reduce (NCCL for CUDA tensors, gloo
+for CPU tensors) per phase.  Every rank takes the same collective steps in the
+same order, because each decision is made from the combined counters.
+"""
+
+from __future__ import annotations
+
+from typing import Protocol, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+class Shard(Protocol):
+    """One shard's staged adjoint; counters are two integers (a tensor or sequence)."""
+
+    def prepare(self): ...  # -> (0, samples above their threshold)
+
+    def cycle(self, completed: int): ...  # -> (Arnoldi steps, samples still above)
+
+    def finish(self): ...  # -> the shard's outputs
+
+
+def combine_max(counters: Sequence, group=None) -> tuple[int, int]:
+    """Elementwise max of the shards' counters here and, with ``group``, on every rank."""
+    acc = None
+    for c in counters:
+        t = torch.as_tensor(c)
+        acc = t.clone() if acc is None else torch.maximum(acc, t.to(acc.device))
+    if acc is None:
+        raise ValueError("combine_max needs at least one shard")
+    if group is not None:
+        dist.all_reduce(acc, op=dist.ReduceOp.MAX, group=group)
+    length, active = (int(v) for v in acc.tolist())
+    return length, active
+
+
+def run(shards: Sequence[Shard], max_iterations: int, group=None):
+    """Run the shards' staged adjoints with the batch-wide GMRES budget.
+
+    Returns ``(outputs, completed, cycles)``: each shard's ``finish()`` result,
+    the Arnoldi steps charged to the shared budget, and the cycles run -- the
+    same on every rank and the same as an unsharded run of the whole batch.
+    """
+    _, active = combine_max([s.prepare() for s in shards], group)
+    completed = 0
+    cycles = 0
+    while completed < max_iterations and active > 0:
+        length, active = combine_max([s.cycle(completed) for s in shards], group)
+        if length <= 0:
+            # An active sample always takes at least one step; a zero here means
+            # no shard ran its cycle.  Every rank sees the same value and stops.
+            raise RuntimeError("lockstep GMRES: an active cycle reported no Arnoldi steps")
+        completed += length
+        cycles += 1
+    return [s.finish() for s in shards], completed, cycles
