@@ -66,7 +66,9 @@ typedef enum PurinDtype { PURIN_FLOAT64 = 0, PURIN_FLOAT32 = 1 } PurinDtype;
 /* Which computation a workspace is sized for. */
 typedef enum PurinCpOp {
   PURIN_CP_OP_FORWARD = 0,
-  PURIN_CP_OP_ADJOINT = 1
+  PURIN_CP_OP_ADJOINT = 1,
+  PURIN_QP_OP_FORWARD = 2, /* purin_qp_forward */
+  PURIN_QP_OP_ADJOINT = 3  /* purin_qp_adjoint */
 } PurinCpOp;
 
 /* Index arrays derived by the plan (purin_cp_plan_indices). */
@@ -275,6 +277,89 @@ int32_t purin_cp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* con
 
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args,
                              void* stream);
+
+/* ---- General diagonal QP ---------------------------------------------------
+ * PreparedDiagonalQP (src/purin/solvers/diagonal_qp.py:72-314) on the same
+ * kernels: minimise 0.5 sum(q y^2) + c.y subject to the equality rows, the
+ * inequality rows (<= rhs) and lower <= y <= upper, with q, c, the row values,
+ * rhs and bounds all per sample and all differentiable.
+ *
+ *   purin_qp_plan_create <- QPStructure.prepare / PreparedDiagonalQP.__post_init__
+ *                           (diagonal_qp.py:64-89): the padded layout of ALL
+ *                           rows (no singleton-row presolve); plan_info reports
+ *                           kept_rows = me + mi and bound_rows = 0.
+ *   purin_qp_forward     <- the custom-VJP solve's forward (diagonal_qp.py:99-131):
+ *                           sparse_cp(q, c, values, rhs, ..., y0, dual0,
+ *                           freeze_converged, check_stationarity), converged &=
+ *                           all(q > 0) & all(lower <= upper).
+ *   purin_qp_adjoint     <- its bwd (diagonal_qp.py:133-222): step sizes
+ *                           (diagonal, norm bound or power iteration; tau =
+ *                           s/(max q + L)), GMRES on (I - J^T) v = (cot_y,
+ *                           cot_dual, 0), pullback to (q, c, values, rhs,
+ *                           lower, upper).
+ * Row scaling and the post-processing of PreparedDiagonalQP.solve
+ * (diagonal_qp.py:225-314) are elementwise and stay with the host layer. */
+int32_t purin_qp_plan_create(const PurinCpStructure* structure, PurinCpPlan** plan);
+
+typedef struct PurinQpForwardArgs {
+  int64_t batch;
+  const void* q;            /* (B, n) diagonal objective                     */
+  const void* c;            /* (B, n) linear objective                       */
+  const void* values;       /* row values, CSR slot order of all rows        */
+  int64_t values_stride;    /* 0 (shared by the batch) or nnz                */
+  const void* rhs;          /* (B, m) equality then inequality rhs           */
+  const void* lower;        /* (B, n) or (n,)                                */
+  const void* upper;
+  int64_t bounds_stride;    /* 0 or n                                        */
+  const void* y0;           /* (B, n) primal warm start, or NULL for zeros   */
+  const void* dual0;        /* (B, m) dual warm start, or NULL for zeros     */
+  const void* tolerance;    /* (B,) per-sample solve tolerance               */
+  int64_t sample_offset;    /* index of sample 0 in the global batch (PRNG)  */
+  int64_t total_batch;      /* global batch size (PRNG key split count)      */
+  void* y;                  /* out (B, n)                                    */
+  void* dual;               /* out (B, m)                                    */
+  int32_t* iterations;      /* out (B,)                                      */
+  void* residual;           /* out (B,)                                      */
+  void* gap;                /* out (B,)                                      */
+  uint8_t* converged;       /* out (B,)                                      */
+} PurinQpForwardArgs;
+
+typedef struct PurinQpAdjointArgs {
+  int64_t batch;
+  const void* q;
+  const void* c;
+  const void* values;
+  int64_t values_stride;
+  const void* rhs;
+  const void* lower;
+  const void* upper;
+  int64_t bounds_stride;
+  const void* y;            /* (B, n) forward solution                       */
+  const void* dual;         /* (B, m) forward duals                          */
+  const uint8_t* converged; /* (B,) forward convergence (after validity)     */
+  const void* cot_y;        /* (B, n) cotangent of y                         */
+  const void* cot_dual;     /* (B, m) cotangent of the duals, or NULL (zero) */
+  int64_t sample_offset;
+  int64_t total_batch;
+  void* grad_q;             /* out (B, n) or NULL                            */
+  void* grad_c;             /* out (B, n) or NULL                            */
+  void* grad_values;        /* out (B, nnz) or NULL                          */
+  void* grad_rhs;           /* out (B, m) or NULL                            */
+  void* grad_lower;         /* out (B, n) or NULL                            */
+  void* grad_upper;         /* out (B, n) or NULL                            */
+  int32_t* linear_status;   /* out (B,) GMRES info 0/1/2, or NULL            */
+  void* linear_residual;    /* out (B,) or NULL                              */
+  int32_t* device_error;    /* out (1,)                                      */
+} PurinQpAdjointArgs;
+
+int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config,
+                         const PurinQpForwardArgs* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+int32_t purin_qp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config,
+                         const PurinLinearSolverConfig* linear,
+                         const PurinQpAdjointArgs* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* purin_cp_forward_noalloc: the forward solve of purin_cp_forward for callers
  * that cannot allocate device memory -- a plugin or custom-call hook that is

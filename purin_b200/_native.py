@@ -16,7 +16,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpurin_cp.so"
 ABI_VERSION = 1
 
 PURIN_FLOAT64, PURIN_FLOAT32 = 0, 1
-OP_FORWARD, OP_ADJOINT = 0, 1
+OP_FORWARD, OP_ADJOINT, QP_OP_FORWARD, QP_OP_ADJOINT = 0, 1, 2, 3
 STAGE_PREPARE, STAGE_CYCLE, STAGE_FINISH = 0, 1, 2
 KEPT_ROWS, KEPT_SLOTS, BOUND_ROWS, BOUND_SLOTS, BOUND_VARIABLES, KEPT_ROW_PTR, KEPT_COLS = range(7)
 
@@ -65,6 +65,25 @@ class AdjointArgs(ctypes.Structure):
                 ("device_error", c_vp)]
 
 
+class QpForwardArgs(ctypes.Structure):
+    _fields_ = [("batch", c_i64), ("q", c_vp), ("c", c_vp), ("values", c_vp),
+                ("values_stride", c_i64), ("rhs", c_vp), ("lower", c_vp), ("upper", c_vp),
+                ("bounds_stride", c_i64), ("y0", c_vp), ("dual0", c_vp), ("tolerance", c_vp),
+                ("sample_offset", c_i64), ("total_batch", c_i64), ("y", c_vp), ("dual", c_vp),
+                ("iterations", c_vp), ("residual", c_vp), ("gap", c_vp), ("converged", c_vp)]
+
+
+class QpAdjointArgs(ctypes.Structure):
+    _fields_ = [("batch", c_i64), ("q", c_vp), ("c", c_vp), ("values", c_vp),
+                ("values_stride", c_i64), ("rhs", c_vp), ("lower", c_vp), ("upper", c_vp),
+                ("bounds_stride", c_i64), ("y", c_vp), ("dual", c_vp), ("converged", c_vp),
+                ("cot_y", c_vp), ("cot_dual", c_vp), ("sample_offset", c_i64),
+                ("total_batch", c_i64), ("grad_q", c_vp), ("grad_c", c_vp),
+                ("grad_values", c_vp), ("grad_rhs", c_vp), ("grad_lower", c_vp),
+                ("grad_upper", c_vp), ("linear_status", c_vp), ("linear_residual", c_vp),
+                ("device_error", c_vp)]
+
+
 class PostArgs(ctypes.Structure):
     _fields_ = [("batch", c_i64), ("values_all", c_vp), ("values_all_stride", c_i64),
                 ("rhs_all", c_vp), ("target", c_vp), ("lower", c_vp), ("upper", c_vp),
@@ -79,7 +98,7 @@ EXPORTED = (
     "purin_cp_abi_version", "purin_cp_last_error", "purin_cp_plan_create",
     "purin_cp_plan_destroy", "purin_cp_plan_info", "purin_cp_plan_indices",
     "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_adjoint_stage",
-    "purin_cp_postprocess",
+    "purin_cp_postprocess", "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
 )
 
 _lib = None
@@ -120,9 +139,15 @@ def load():
                                            ctypes.POINTER(AdjointArgs), c_i32, c_i32, c_vp, c_vp,
                                            ctypes.c_size_t, c_vp]
     lib.purin_cp_postprocess.argtypes = [c_vp, ctypes.POINTER(PostArgs), c_vp]
+    lib.purin_qp_plan_create.argtypes = [ctypes.POINTER(Structure), ctypes.POINTER(c_vp)]
+    lib.purin_qp_forward.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(QpForwardArgs),
+                                     c_vp, ctypes.c_size_t, c_vp]
+    lib.purin_qp_adjoint.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(LinearConfig),
+                                     ctypes.POINTER(QpAdjointArgs), c_vp, ctypes.c_size_t, c_vp]
     for name in ("purin_cp_plan_create", "purin_cp_plan_destroy", "purin_cp_plan_info",
                  "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward",
-                 "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess"):
+                 "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess",
+                 "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint"):
         getattr(lib, name).restype = c_i32
     version = lib.purin_cp_abi_version()
     if version != ABI_VERSION:
@@ -140,7 +165,7 @@ def check(status: int, what: str):
 class Plan:
     """Owning handle of a ``PurinCpPlan`` (immutable device-resident structure)."""
 
-    def __init__(self, n, me, mi, row_ptr, col, dtype_code, device):
+    def __init__(self, n, me, mi, row_ptr, col, dtype_code, device, qp=False):
         lib = load()
         self._lib = lib
         self._row_ptr = np.ascontiguousarray(row_ptr, dtype=np.int32)
@@ -151,7 +176,8 @@ class Plan:
                       self._row_ptr.ctypes.data_as(c_i32p), self._col.ctypes.data_as(c_i32p),
                       int(dtype_code), int(device))
         handle = c_vp()
-        check(lib.purin_cp_plan_create(ctypes.byref(s), ctypes.byref(handle)), "purin_cp_plan_create")
+        create = "purin_qp_plan_create" if qp else "purin_cp_plan_create"
+        check(getattr(lib, create)(ctypes.byref(s), ctypes.byref(handle)), create)
         self.handle = handle
         info = PlanInfo()
         check(lib.purin_cp_plan_info(handle, ctypes.byref(info)), "purin_cp_plan_info")
@@ -192,6 +218,15 @@ class Plan:
                                                ctypes.byref(args), stage, completed, counters_ptr,
                                                workspace_ptr, workspace_bytes, stream),
               "purin_cp_adjoint_stage")
+
+    def qp_forward(self, cfg, args, workspace_ptr, workspace_bytes, stream):
+        check(self._lib.purin_qp_forward(self.handle, ctypes.byref(cfg), ctypes.byref(args),
+                                         workspace_ptr, workspace_bytes, stream), "purin_qp_forward")
+
+    def qp_adjoint(self, cfg, lin, args, workspace_ptr, workspace_bytes, stream):
+        check(self._lib.purin_qp_adjoint(self.handle, ctypes.byref(cfg), ctypes.byref(lin),
+                                         ctypes.byref(args), workspace_ptr, workspace_bytes,
+                                         stream), "purin_qp_adjoint")
 
     def postprocess(self, args, stream):
         check(self._lib.purin_cp_postprocess(self.handle, ctypes.byref(args), stream),

@@ -61,17 +61,18 @@ struct FwdPlan {
   size_t workspace = 0;  // total bytes
   size_t off_vr = 0, off_vc = 0, off_state = 0;
   size_t off_tgt = 0, off_rhs = 0, off_dual0 = 0, off_lo = 0, off_up = 0;
+  size_t off_q = 0, off_c = 0, off_y0 = 0;  // diagonal QP inputs (internal order)
   int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
 
 FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
-                           bool shared_values);
+                           bool shared_values, bool qp);
 
 // The workspace does not depend on shared_values: it only ranks tile widths
 // whose state fits in shared memory, which need no workspace for the state.
 FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
-                     bool shared_values = true) {
-  FwdPlan fp = plan_forward_tiles(const_cast<PurinCpPlan*>(plan), cfg, batch, shared_values);
+                     bool shared_values = true, bool qp = false) {
+  FwdPlan fp = plan_forward_tiles(const_cast<PurinCpPlan*>(plan), cfg, batch, shared_values, qp);
   const size_t w = dtype_size(plan->info.dtype);
   fp.sell_index = 0;  // one lane per line: slices of C = 32 for every tile width
   const purin::SellView& sv = plan->sell[fp.sell_index];
@@ -85,20 +86,27 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   fp.off_dual0 = fp.off_rhs + align_up(nb * sv.m_pos * w);
   fp.off_lo = fp.off_dual0 + align_up(nb * sv.m_pos * w);
   fp.off_up = fp.off_lo + align_up(nb * sv.n_pos * w);
-  fp.off_state = fp.off_up + align_up(nb * sv.n_pos * w);
+  // The diagonal QP's q, c and y0 follow; the distance projection needs none.
+  const size_t qp_vec = qp ? align_up(nb * sv.n_pos * w) : 0;
+  fp.off_q = fp.off_up + align_up(nb * sv.n_pos * w);
+  fp.off_c = fp.off_q + qp_vec;
+  fp.off_y0 = fp.off_c + qp_vec;
+  fp.off_state = fp.off_y0 + qp_vec;
   fp.workspace = fp.off_state + fp.workspace;
   return fp;
 }
 
 FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
-                           bool shared_values) {
+                           bool shared_values, bool qp) {
   FwdPlan fp;
   const size_t w = dtype_size(plan->info.dtype);
   const bool f64 = plan->info.dtype == PURIN_FLOAT64;
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
+  // Per-variable proximal coefficients: diagonal steps, or a fixed-step QP.
+  const bool pv = diag || (qp && !cfg->accelerated);
   const int n_pos = plan->sell[0].n_pos, m_pos = plan->sell[0].m_pos;
   const size_t per_sample =
-      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * w;
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) : 0) + (diag ? (m_pos + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
@@ -116,6 +124,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   int64_t best_warps = -1, best_samples = -1;
   for (int k = 0; k < 6; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
+    if (qp && S != 1) continue;  // the QP kernels are built for one-sample tiles
     const size_t stat = f64 ? purin::forward_static_smem<double>(S, NT)
                             : purin::forward_static_smem<float>(S, NT);
     // Shared-memory tiles read the 16-bit index pairs (always present when a
@@ -127,11 +136,11 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
       if (NT == want_nt && S <= want_s && (best < 0 || S > kShapes[best][0])) best = k;
       continue;
     }
-    int& cached = plan->fwd_blocks[diag ? 1 : 0][shared_values ? 1 : 0][k];
+    int& cached = plan->fwd_blocks[qp ? (pv ? 3 : 2) : (diag ? 1 : 0)][shared_values ? 1 : 0][k];
     if (cached < 0) {
       const size_t dyn = (size_t)S * per_sample;
-      cached = f64 ? purin::forward_blocks_per_sm<double>(S, NT, shared_values, dyn)
-                   : purin::forward_blocks_per_sm<float>(S, NT, shared_values, dyn);
+      cached = f64 ? purin::forward_blocks_per_sm<double>(S, NT, shared_values, dyn, qp)
+                   : purin::forward_blocks_per_sm<float>(S, NT, shared_values, dyn, qp);
     }
     const int64_t tiles = (batch + S - 1) / S;
     const int64_t ctas = std::min<int64_t>(tiles, sms * std::max(cached, 0));
@@ -150,7 +159,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
     fp.smem_bytes = (size_t)fp.S * per_sample;
     fp.workspace = 0;
   } else {
-    fp.S = 8;
+    fp.S = qp ? 1 : 8;
     fp.NT = purin::kForwardThreads;
     fp.smem = false;
     fp.smem_bytes = 0;
@@ -169,7 +178,7 @@ struct AdjLayout {
 };
 
 AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
-                       const PurinLinearSolverConfig* lin, int64_t batch) {
+                       const PurinLinearSolverConfig* lin, int64_t batch, bool qp = false) {
   AdjLayout L;
   const int n = plan->info.n, m = plan->info.kept_rows;
   const int64_t W = 2 * (int64_t)n + m;
@@ -192,7 +201,9 @@ AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
   L.off_x = take((size_t)batch * W * w);
   L.off_lamp = take((size_t)batch * m * w);
   L.off_steps = take((size_t)batch * 2 * w);
-  L.off_dsteps = take(diag ? (size_t)batch * (2 * n + m) * w : 0);
+  // Per-variable steps: diagonal preconditioning, or every diagonal QP
+  // (a_j, d_j depend on q_j; tau per column follows for the q cotangent).
+  L.off_dsteps = take(qp ? (size_t)batch * (3 * n + m) * w : diag ? (size_t)batch * (2 * n + m) * w : 0);
   L.off_thresh = take((size_t)batch * w);
   L.off_resinf = take((size_t)batch * w);
   L.off_basis = take((size_t)std::max(L.grid, 1) * (L.R + 1) * W * w);
@@ -228,11 +239,20 @@ int32_t check_linear(const PurinLinearSolverConfig* lin) {
   return PURIN_OK;
 }
 
+// The diagonal QP's extra forward inputs (purin_qp_forward); null for the
+// distance projection.
+struct QpInputs {
+  const void* q;
+  const void* c;
+  const void* y0;
+};
+
 template <typename T>
 int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinCpForwardArgs* a,
-                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                    void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                    const QpInputs* qp = nullptr) {
   const bool shared = a->values_stride == 0 || a->batch == 1;
-  const FwdPlan fp = plan_forward(plan, cfg, a->batch, shared);
+  const FwdPlan fp = plan_forward(plan, cfg, a->batch, shared, qp != nullptr);
   if (workspace == nullptr || workspace_bytes < fp.workspace)
     return fail(PURIN_ERR_WORKSPACE, "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes");
   char* ws = static_cast<char*>(workspace);
@@ -255,10 +275,24 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   T* lo_i = reinterpret_cast<T*>(ws + fp.off_lo);
   T* up_i = reinterpret_cast<T*>(ws + fp.off_up);
   const int64_t bound_rows = a->bounds_stride == 0 ? 1 : a->batch;
+  T* q_i = qp ? reinterpret_cast<T*>(ws + fp.off_q) : nullptr;
+  T* c_i = qp ? reinterpret_cast<T*>(ws + fp.off_c) : nullptr;
+  T* y0_i = (qp && qp->y0) ? reinterpret_cast<T*>(ws + fp.off_y0) : nullptr;
   {
     const int n = plan->info.n, m = plan->info.kept_rows;
-    cudaError_t e = purin::permute_rows<T>(static_cast<const T*>(a->target), n, sv.c_perm, sv.n_pos,
-                                           a->batch, tgt_i, stream);
+    cudaError_t e = cudaSuccess;
+    if (qp) {
+      e = purin::permute_rows<T>(static_cast<const T*>(qp->q), n, sv.c_perm, sv.n_pos, a->batch, q_i, stream);
+      if (e == cudaSuccess)
+        e = purin::permute_rows<T>(static_cast<const T*>(qp->c), n, sv.c_perm, sv.n_pos, a->batch, c_i,
+                                   stream);
+      if (e == cudaSuccess && y0_i)
+        e = purin::permute_rows<T>(static_cast<const T*>(qp->y0), n, sv.c_perm, sv.n_pos, a->batch, y0_i,
+                                   stream);
+    } else {
+      e = purin::permute_rows<T>(static_cast<const T*>(a->target), n, sv.c_perm, sv.n_pos, a->batch, tgt_i,
+                                 stream);
+    }
     if (e == cudaSuccess && m > 0)
       e = purin::permute_rows<T>(static_cast<const T*>(a->rhs), m, sv.r_perm, sv.m_pos, a->batch,
                                  rhs_i, stream);
@@ -276,7 +310,10 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
     if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward input layout");
   }
   purin::FwdParams<T> p{};
-  p.tgt_i = tgt_i;
+  p.tgt_i = qp ? nullptr : tgt_i;
+  p.q_i = q_i;
+  p.c_i = c_i;
+  p.y0_i = y0_i;
   p.rhs_i = rhs_i;
   p.dual0_i = (dual0_i && plan->info.kept_rows > 0) ? dual0_i : nullptr;
   p.lo_i = lo_i;
@@ -378,11 +415,20 @@ purin::AdjParams<T> adjoint_params(const PurinCpPlan* plan, const PurinCpConfig*
   return p;
 }
 
+// The diagonal QP's extra adjoint inputs and outputs (purin_qp_adjoint).
+struct QpAdjoint {
+  const void* q;
+  const void* c;
+  const void* cot_dual;
+  void* grad_q;
+  void* grad_c;
+};
+
 template <typename T>
 int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                     const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
-                    cudaStream_t stream) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
+                    cudaStream_t stream, const QpAdjoint* qp = nullptr) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -392,7 +438,16 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
   e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
-  const purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
+  purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
+  if (qp) {
+    p.qp = 1;
+    p.q = static_cast<const T*>(qp->q);
+    p.c = static_cast<const T*>(qp->c);
+    p.cot_dual = static_cast<const T*>(qp->cot_dual);
+    p.g_q = static_cast<T*>(qp->grad_q);
+    p.g_c = static_cast<T*>(qp->grad_c);
+    p.norm_bound = cfg->norm_bound ? 1 : 0;
+  }
   e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch");
   return PURIN_OK;
@@ -557,6 +612,8 @@ int32_t check_adjoint_args(const PurinCpPlan* plan, const PurinCpAdjointArgs* ar
     return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
   return PURIN_OK;
 }
+
+int32_t create_plan(const PurinCpStructure* s, PurinCpPlan** out, bool presolve_bounds);
 }  // namespace
 
 extern "C" {
@@ -566,6 +623,17 @@ int32_t purin_cp_abi_version(void) { return PURIN_CP_ABI_VERSION; }
 const char* purin_cp_last_error(void) { return g_last_error.c_str(); }
 
 int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
+  return create_plan(s, out, true);
+}
+
+int32_t purin_qp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
+  return create_plan(s, out, false);
+}
+
+}  // extern "C"
+
+namespace {
+int32_t create_plan(const PurinCpStructure* s, PurinCpPlan** out, bool presolve_bounds) {
   if (!s || !out) return fail(PURIN_ERR_INVALID_ARGUMENT, "structure and output pointers are required");
   *out = nullptr;
   const int n = s->n, me = s->equality_size, mi = s->inequality_size;
@@ -603,9 +671,10 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
   for (int i = 0; i < m_all; ++i) width = std::max(width, row_ptr[i + 1] - row_ptr[i]);
   info.width = width;
 
-  // prepare_bounds (bounds.py:320-326): singleton inequality rows.
+  // prepare_bounds (bounds.py:320-326): singleton inequality rows.  The
+  // diagonal QP keeps every row (diagonal_qp.py:88 lays out all rows).
   std::vector<char> is_bound(m_all, 0);
-  for (int i = 0; i < mi; ++i) {
+  for (int i = 0; presolve_bounds && i < mi; ++i) {
     const int r = me + i;
     if (row_ptr[r + 1] - row_ptr[r] == 1) {
       is_bound[r] = 1;
@@ -800,6 +869,9 @@ int32_t purin_cp_plan_create(const PurinCpStructure* s, PurinCpPlan** out) {
   *out = plan;
   return PURIN_OK;
 }
+}  // namespace
+
+extern "C" {
 
 int32_t purin_cp_plan_destroy(PurinCpPlan* plan) {
   if (!plan) return PURIN_OK;
@@ -851,9 +923,13 @@ int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t bat
     *bytes = plan_forward(plan, config, batch).workspace;
     return PURIN_OK;
   }
-  if (op == PURIN_CP_OP_ADJOINT) {
+  if (op == PURIN_QP_OP_FORWARD) {
+    *bytes = plan_forward(plan, config, batch, true, true).workspace;
+    return PURIN_OK;
+  }
+  if (op == PURIN_CP_OP_ADJOINT || op == PURIN_QP_OP_ADJOINT) {
     if (int32_t r = check_linear(linear)) return r;
-    const AdjLayout L = plan_adjoint(plan, config, linear, batch);
+    const AdjLayout L = plan_adjoint(plan, config, linear, batch, op == PURIN_QP_OP_ADJOINT);
     if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
     *bytes = L.total;
     return PURIN_OK;
@@ -932,6 +1008,97 @@ int32_t purin_cp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, c
   return plan->info.dtype == PURIN_FLOAT64
              ? run_adjoint<double>(plan, config, linear, args, workspace, workspace_bytes, s)
              : run_adjoint<float>(plan, config, linear, args, workspace, workspace_bytes, s);
+}
+
+int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinQpForwardArgs* args,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (plan->info.bound_rows != 0)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "purin_qp_forward needs a plan from purin_qp_plan_create");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  const int m = plan->info.kept_rows;
+  if (!args->q || !args->c || !args->tolerance || !args->lower || !args->upper || !args->y ||
+      !args->iterations || !args->residual || !args->gap || !args->converged ||
+      (m > 0 && (!args->rhs || !args->dual)) || (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required QP forward array is NULL");
+  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or nnz");
+  if (args->bounds_stride != 0 && args->bounds_stride != plan->info.n)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "bounds_stride must be 0 or n");
+  PurinCpForwardArgs a{};
+  a.batch = args->batch;
+  a.values = args->values;
+  a.values_stride = args->values_stride;
+  a.rhs = args->rhs;
+  a.target = nullptr;
+  a.dual0 = args->dual0;
+  a.tolerance = args->tolerance;
+  a.lower = args->lower;
+  a.upper = args->upper;
+  a.bounds_stride = args->bounds_stride;
+  a.feasible = nullptr;
+  a.sample_offset = args->sample_offset;
+  a.total_batch = args->total_batch;
+  a.y = args->y;
+  a.dual = args->dual;
+  a.iterations = args->iterations;
+  a.residual = args->residual;
+  a.gap = args->gap;
+  a.converged = args->converged;
+  const QpInputs qp{args->q, args->c, args->y0};
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64
+             ? run_forward<double>(plan, config, &a, workspace, workspace_bytes, s, &qp)
+             : run_forward<float>(plan, config, &a, workspace, workspace_bytes, s, &qp);
+}
+
+int32_t purin_qp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
+                         const PurinQpAdjointArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (plan->info.bound_rows != 0)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "purin_qp_adjoint needs a plan from purin_qp_plan_create");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  if (!args->q || !args->c) return fail(PURIN_ERR_INVALID_ARGUMENT, "a required QP adjoint array is NULL");
+  PurinCpAdjointArgs a{};
+  a.batch = args->batch;
+  a.values = args->values;
+  a.values_stride = args->values_stride;
+  a.rhs = args->rhs;
+  a.target = args->c;  // satisfies the shared check; the QP kernels read c through QpAdjoint
+  a.lower = args->lower;
+  a.upper = args->upper;
+  a.bounds_stride = args->bounds_stride;
+  a.y = args->y;
+  a.dual = args->dual;
+  a.converged = args->converged;
+  a.cot_y = args->cot_y;
+  a.sample_offset = args->sample_offset;
+  a.total_batch = args->total_batch;
+  a.grad_values = args->grad_values;
+  a.grad_rhs = args->grad_rhs;
+  a.grad_target = nullptr;
+  a.grad_lower = args->grad_lower;
+  a.grad_upper = args->grad_upper;
+  a.linear_status = args->linear_status;
+  a.linear_residual = args->linear_residual;
+  a.device_error = args->device_error;
+  if (int32_t r = check_adjoint_args(plan, &a)) return r;
+  const QpAdjoint qp{args->q, args->c, args->cot_dual, args->grad_q, args->grad_c};
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64
+             ? run_adjoint<double>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp)
+             : run_adjoint<float>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp);
 }
 
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args, void* stream) {

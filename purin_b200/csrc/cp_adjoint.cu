@@ -81,6 +81,20 @@ __device__ T block_max(T v, T* red) {
   __syncthreads();
   return total;
 }
+// Block-wide max whose identity is -inf (block_max starts from 0, which suits
+// nonnegative quantities only).
+template <typename T>
+__device__ T block_max_from(T v, T* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  T total = red[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) total = pmax(total, red[w]);
+  __syncthreads();
+  return total;
+}
 __device__ __forceinline__ int block_and(int v) {
   return __syncthreads_and(v);
 }
@@ -95,7 +109,9 @@ struct Sample {
   const T* ys;     // forward solution y* (also ybar at the linearisation point)
   const T* ds;     // forward duals
   const T* cot;    // cotangent of y
+  const T* cotd;   // cotangent of the duals (QP), or null
   bool conv;
+  bool qp;         // tgt holds c (diagonal QP) instead of the target (c = -target)
   T* lamp;         // lambda+ at the linearisation point
   uint8_t* yc;     // per-column derivative codes
   uint8_t* dc;     // per-row derivative codes
@@ -110,23 +126,26 @@ __device__ Sample<T> make_sample(const AdjParams<T>& p, int64_t X) {
   const int n = p.st.n, m = p.st.m;
   Sample<T> s;
   s.vals = p.values + X * p.values_stride;
-  s.tgt = p.target + X * n;
+  s.qp = p.qp != 0;
+  s.tgt = s.qp ? p.c + X * n : p.target + X * n;
   s.rhs = p.rhs + X * m;
   s.lo = p.lower + X * p.bounds_stride;
   s.up = p.upper + X * p.bounds_stride;
   s.ys = p.y + X * n;
   s.ds = p.dual + X * m;
   s.cot = p.cot_y + X * n;
+  s.cotd = p.cot_dual ? p.cot_dual + X * m : nullptr;
   s.conv = p.converged[X] != 0;
   s.lamp = p.lamp + X * m;
   s.yc = p.ycode + X * n;
   s.dc = p.dcode + X * m;
-  if (p.diag) {
-    T* base = p.dsteps + X * (2 * (int64_t)n + m);
+  if (p.diag || p.qp) {
+    T* base = p.dsteps + X * ((p.qp ? 3 : 2) * (int64_t)n + m);
     s.av = base;
     s.dv = base + n;
-    s.sv = base + 2 * n;
-    s.a = s.d = s.sigma = T(0);
+    s.sv = p.diag ? base + 2 * n : nullptr;
+    s.a = s.d = T(0);
+    s.sigma = p.diag ? T(0) : p.steps[2 * X + 1];
   } else {
     const T tau = p.steps[2 * X], sigma = p.steps[2 * X + 1];
     s.a = T(1) / (T(1) + tau * T(1));
@@ -173,10 +192,13 @@ __device__ void apply_operator(const DevStructure& st, const Sample<T>& s, T* bu
   __syncthreads();
 }
 
-// g = (where(converged, cot_y, 0), 0, 0) entry e.
+// g = (where(converged, cot_y, 0), where(converged, cot_dual, 0), 0) entry e
+// (bounds.py:131-138; diagonal_qp.py:191-196 adds the dual cotangent).
 template <typename T>
-__device__ __forceinline__ T rhs_entry(const Sample<T>& s, int n, int e) {
-  return (e < n && s.conv) ? s.cot[e] : T(0);
+__device__ __forceinline__ T rhs_entry(const Sample<T>& s, int n, int m, int e) {
+  if (!s.conv) return T(0);
+  if (e < n) return s.cot[e];
+  return (s.cotd && e < n + m) ? s.cotd[e - n] : T(0);
 }
 
 // Dot products of buf with basis rows [0, r) into out[0, r) (CGS pass, first half).
@@ -249,6 +271,29 @@ __device__ __forceinline__ T jax_hypot(T x, T y) {
   return inf ? T(INFINITY) : r;
 }
 
+// Diagonal-QP backward steps (diagonal_qp.py:149-150): tau = s/(max q + L),
+// sigma = s/L, and the proximal coefficients a_j = 1/(1 + tau q_j), d_j = tau a_j
+// of the step whose pullback is taken (kernels.py:68-73).
+template <typename T>
+__device__ void qp_steps(const AdjParams<T>& p, int64_t X, const T* qx, T* base, T L, T* red) {
+  const int n = p.st.n, m = p.st.m;
+  T qmax = T(-INFINITY);
+  for (int j = threadIdx.x; j < n; j += kThreads) qmax = pmax(qmax, qx[j]);
+  qmax = block_max_from(qmax, red);
+  const T tau = p.safety / (qmax + L);
+  for (int j = threadIdx.x; j < n; j += kThreads) {
+    const T a = T(1) / (T(1) + tau * qx[j]);
+    base[j] = a;
+    base[n + j] = tau * a;
+    base[2 * n + m + j] = tau;
+  }
+  if (threadIdx.x == 0) {
+    p.steps[2 * X] = tau;
+    p.steps[2 * X + 1] = p.safety / L;
+  }
+  __syncthreads();
+}
+
 template <typename T, bool kSmem>
 __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T> p) {
   extern __shared__ __align__(16) unsigned char dyn[];
@@ -298,8 +343,9 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       continue;
     }
     const T* vals = p.values + X * p.values_stride;
+    const T* qx = p.qp ? p.q + X * n : nullptr;
+    T* base = (p.diag || p.qp) ? p.dsteps + X * ((p.qp ? 3 : 2) * (int64_t)n + m) : nullptr;
     if (p.diag) {
-      T* base = p.dsteps + X * (2 * (int64_t)n + m);
       for (int i = threadIdx.x; i < m; i += kThreads) {
         T acc = zero;
         for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + fabs(vals[k]) * one;
@@ -310,10 +356,29 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
           acc = acc + fabs(vals[st.csc_slot[e]]) * one;
         const T tau = p.safety / (acc > zero ? pmax(acc, T(1e-12)) : one);
-        const T a = one / (one + tau * one);
+        const T a = one / (one + tau * (qx ? qx[j] : one));
         base[j] = a;
         base[n + j] = tau * a;
+        if (p.qp) base[2 * n + m + j] = tau;
       }
+    } else if (p.qp && p.norm_bound) {
+      // L = sqrt(max row sum |K| * max column sum |K|) (diagonal_qp.py:143-148).
+      T rmax = zero, cmax = zero;
+      for (int i = threadIdx.x; i < m; i += kThreads) {
+        T acc = zero;
+        for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + fabs(vals[k]) * one;
+        rmax = pmax(rmax, acc);
+      }
+      for (int j = threadIdx.x; j < n; j += kThreads) {
+        T acc = zero;
+        for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+          acc = acc + fabs(vals[st.csc_slot[e]]) * one;
+        cmax = pmax(cmax, acc);
+      }
+      rmax = block_max(rmax, red);
+      cmax = block_max(cmax, red);
+      const T L = pmax(sqrt(rmax * cmax), T(1e-12));
+      qp_steps(p, X, qx, base, L, red);
     } else {
       uint32_t k0, k1;
       split_key(p.norm_seed, p.sample_offset + X, p.total_batch, p.partitionable != 0, k0, k1);
@@ -349,7 +414,9 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         for (int j = threadIdx.x; j < n; j += kThreads) x[j] = tn[j] / zn;
       }
       const T L = pmax(sqrt(pmax(eig, zero)) + T(1e-12), T(1e-12));
-      if (threadIdx.x == 0) {
+      if (p.qp) {
+        qp_steps(p, X, qx, base, L, red);
+      } else if (threadIdx.x == 0) {
         p.steps[2 * X] = p.safety / (one + L);
         p.steps[2 * X + 1] = p.safety / L;
       }
@@ -373,7 +440,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
         t = t + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
       const T yo = s.ys[j];
-      const T c = -s.tgt[j];
+      const T c = s.qp ? s.tgt[j] : -s.tgt[j];
       const T aa = s.av ? s.av[j] : s.a;
       const T dd = s.dv ? s.dv[j] : s.d;
       const T yr = (aa * yo - dd * t) + (-dd) * c;
@@ -390,14 +457,14 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     // Right-hand side scale, threshold, x = 0 and the initial residual.
     T gmax = zero;
     for (int e = threadIdx.x; e < W; e += kThreads) {
-      gmax = pmax(gmax, fabs(rhs_entry(s, n, e)));
+      gmax = pmax(gmax, fabs(rhs_entry(s, n, m, e)));
       buf[e] = zero;
       p.x[X * W + e] = zero;
     }
     gmax = block_max(gmax, red);
     apply_operator(st, s, buf, tn, tm);
     T r0 = zero;
-    for (int e = threadIdx.x; e < W; e += kThreads) r0 = pmax(r0, fabs(rhs_entry(s, n, e) - buf[e]));
+    for (int e = threadIdx.x; e < W; e += kThreads) r0 = pmax(r0, fabs(rhs_entry(s, n, m, e) - buf[e]));
     r0 = block_max(r0, red);
     if (threadIdx.x == 0) {
       const T thr = pmax(p.lin_atol, p.lin_tol * gmax);
@@ -433,7 +500,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       apply_operator(st, s, buf, tn, tm);
       T ss = zero;
       for (int e = threadIdx.x; e < W; e += kThreads) {
-        const T r = rhs_entry(s, n, e) - buf[e];
+        const T r = rhs_entry(s, n, m, e) - buf[e];
         buf[e] = r;
         ss = ss + r * r;
       }
@@ -528,7 +595,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       __syncthreads();
       apply_operator(st, s, buf, tn, tm);
       T cn = zero;
-      for (int e = threadIdx.x; e < W; e += kThreads) cn = pmax(cn, fabs(rhs_entry(s, n, e) - buf[e]));
+      for (int e = threadIdx.x; e < W; e += kThreads) cn = pmax(cn, fabs(rhs_entry(s, n, m, e) - buf[e]));
       cn = block_max(cn, red);
       if (threadIdx.x == 0) {
         p.resinf[X] = cn;
@@ -555,6 +622,8 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         if (p.g_target) p.g_target[X * n + j] = zero;
         if (p.g_lower) p.g_lower[X * n + j] = zero;
         if (p.g_upper) p.g_upper[X * n + j] = zero;
+        if (p.g_q) p.g_q[X * n + j] = zero;
+        if (p.g_c) p.g_c[X * n + j] = zero;
       }
       for (int i = threadIdx.x; i < m; i += kThreads)
         if (p.g_rhs) p.g_rhs[X * m + i] = zero;
@@ -595,6 +664,21 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       const T glo = gg * code_factor<T>((code_j >> 2) & 3);
       const T gup = gg * balanced_factor<T>((code_j >> 4) & 3);
       const T dd = s.dv ? s.dv[j] : s.d;
+      if (s.qp) {
+        // Cotangents of c and q through proximal_coefficients (kernels.py:68-73):
+        // offset = (-d) c, d = tau a, a = 1 / (1 + tau q), and y_raw = a y - d t + offset
+        // with t = K^T lambda+ at the linearisation point, transposed as JAX does
+        // (the reciprocal's cotangent is -(ct * (den * den)^-1)).
+        T tj = zero;
+        for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+          tj = tj + s.vals[st.csc_slot[e]] * s.lamp[st.csc_row[e]];
+        const T tauj = p.dsteps[X * (3 * (int64_t)n + m) + 2 * n + m + j];
+        const T dwbar = ((-graw) * tj) + (-(graw * s.tgt[j]));
+        const T invbar = (graw * s.ys[j]) + (tauj * dwbar);
+        const T den = one + tauj * p.q[X * n + j];
+        if (p.g_q) p.g_q[X * n + j] = clean(tauj * (-((invbar * (one / (den * den))) * one)));
+        if (p.g_c) p.g_c[X * n + j] = clean((-dd) * graw);
+      }
       tn[j] = dd * (-graw);
       if (p.g_target) p.g_target[X * n + j] = clean(dd * graw);
       if (p.g_lower) p.g_lower[X * n + j] = clean(glo);

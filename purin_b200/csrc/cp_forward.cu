@@ -1,7 +1,11 @@
 // Forward CP solve: sparse_cp (src/purin/solvers/chambolle_pock/kernels.py:178-305)
-// with q = 1, c = -target, y0 = target, freeze_converged and check_stationarity on,
-// as called by BoundProjection (bounds.py:42-66) and the unbounded layer
-// (solver.py:149-176).
+// with freeze_converged and check_stationarity on.  The distance projection
+// (kQP false) has q = 1, c = -target, y0 = target, as called by BoundProjection
+// (bounds.py:42-66) and the unbounded layer (solver.py:149-176); the general
+// diagonal QP (kQP true) reads per-sample q, c and y0 (diagonal_qp.py:99-123),
+// with the step sizes, proximal coefficients, stationarity, dual minimiser and
+// acceleration that depend on q (kernels.py:68-73,153-175,209-227,279-283)
+// and converged &= all(q > 0) & all(lower <= upper).
 //
 // One CTA owns a tile of S samples for the whole solve.  The tile's iterates
 // y, ybar (n each) and the duals (m) live in shared memory, interleaved by
@@ -49,6 +53,8 @@ struct TileScratch {
   int active[S], count[S], conv[S];
   T gap_it[S], stat_it[S], resb_it[S];
   int fin_it[S], need_c[S];
+  T gam[S];     // min q (the accelerated update's strong-convexity modulus)
+  int valid[S]; // diagonal QP: all(q > 0) & all(lower <= upper)
   T red[kWarps][S][6];
   int redf[kWarps][S];
   T s_red[kWarps][S];
@@ -207,6 +213,18 @@ __device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
   }
 }
 
+// Minimiser of 0.5 q m^2 + t m over [l, u] (kernels.py:164-169): clip(-t/q)
+// where q > 1e-12, else the bound that t points away from.  With q = 1
+// (distance projection) it is clip(-t/1).
+template <bool kQP, typename T>
+__device__ __forceinline__ T dual_minimiser(T tt, T qj, T l, T u) {
+  if constexpr (kQP) {
+    return qj > T(1e-12) ? clip(-tt / qj, l, u) : (tt >= T(0) ? l : u);
+  } else {
+    return clip(-tt / qj, l, u);
+  }
+}
+
 // Resident CTAs per SM the register budget is sized for (64 registers per
 // thread for one-sample tiles): 1 x 1024, 2 x 512, or 4 / 2 / 1 CTAs of 256
 // threads for S = 1 / 2 / wider.
@@ -214,7 +232,7 @@ constexpr int forward_min_blocks(int S, int NT) {
   return NT >= 1024 ? 1 : NT >= 512 ? 2 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
 }
 
-template <typename T, int S, int NT, bool kSmem, bool kShared>
+template <typename T, int S, int NT, bool kSmem, bool kShared, bool kQP>
 __global__ void __launch_bounds__(NT, forward_min_blocks(S, NT))
 cp_forward_kernel(const FwdParams<T> p) {
   constexpr int kThreads = NT;
@@ -237,15 +255,18 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
   for (int q = 0; q < S; ++q) vals_q[q] = p.values + sample(q) * p.values_stride;
 
+  // Per-variable proximal coefficients live in shared memory for diagonal
+  // steps and for a fixed-step diagonal QP (1 / (1 + tau q_j) differs per variable).
+  const bool pv = p.diag || (kQP && !p.accelerated);
   // Iterates in internal positions: y, ybar (n_pos + 1), duals (m_pos + 1); the
   // last element of each is the zero that padding entries gather.
   const size_t tile_elems =
-      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (p.diag ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * S;
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) : 0) + (p.diag ? (m_pos + 1) : 0)) * S;
   T* base = kSmem ? reinterpret_cast<T*>(dyn_smem) : p.gstate + (size_t)blockIdx.x * tile_elems;
   T* y = base;
   T* ybar = y + (size_t)(n_pos + 1) * S;
   T* lam = ybar + (size_t)(n_pos + 1) * S;
-  T* av = lam + (size_t)(m_pos + 1) * S;  // diagonal steps (only when p.diag)
+  T* av = lam + (size_t)(m_pos + 1) * S;  // per-variable a, d (only when pv); sigma (p.diag)
   T* dv = av + (size_t)(n_pos + 1) * S;
   T* sv_ = dv + (size_t)(n_pos + 1) * S;
 
@@ -278,7 +299,8 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
       for (int q = 0; q < S; ++q) {
         const T tau = safety / (acc[q] > zero ? pmax(acc[q], T(1e-12)) : one);
-        const T a = one / (one + tau * one);
+        const T qj = kQP ? p.q_i[sample(q) * n_pos + pp] : one;
+        const T a = one / (one + tau * qj);
         av[(size_t)pp * S + q] = a;
         dv[(size_t)pp * S + q] = tau * a;
       }
@@ -369,11 +391,60 @@ cp_forward_kernel(const FwdParams<T> p) {
     __syncthreads();
   }
 
-  // ---- initial state: y = ybar = target, lambda = dual0 --------------------
+  // ---- q-dependent scalars (kernels.py:221-227): min q, max q, and the QP's
+  // validity; tau = s/L when accelerated with min q > 0, else s/(max q + L).
+  T qmin[S], qmax[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) qmin[q] = qmax[q] = one;
+  if constexpr (kQP) {
+    T nmin[S], bad[S];
+#pragma unroll
+    for (int q = 0; q < S; ++q) {
+      nmin[q] = T(-INFINITY);  // max of -q: min q without a separate min reduction
+      qmax[q] = T(-INFINITY);
+      bad[q] = zero;
+    }
+    for (int pp = tid; pp < n_pos; pp += kThreads) {
+      if (__ldg(sv.c_perm + pp) < 0) continue;
+#pragma unroll
+      for (int q = 0; q < S; ++q) {
+        const int64_t b = sample(q);
+        const T qj = p.q_i[b * n_pos + pp];
+        nmin[q] = pmax(nmin[q], -qj);
+        qmax[q] = pmax(qmax[q], qj);
+        if (!(p.lo_i[b * p.bstride_i + pp] <= p.up_i[b * p.bstride_i + pp])) bad[q] = one;
+      }
+    }
+    tile_reduce<T, S, true>(nmin, sc.s_red);
+    tile_reduce<T, S, true>(qmax, sc.s_red);
+    tile_reduce<T, S, true>(bad, sc.s_red);
+#pragma unroll
+    for (int q = 0; q < S; ++q) {
+      qmin[q] = -nmin[q];
+      if (tid == 0) sc.valid[q] = (qmin[q] > zero && bad[q] == zero) ? 1 : 0;
+    }
+    if (!p.diag && !p.accelerated) {
+      // Fixed-step proximal coefficients (kernels.py:68-73, precomputed at 236).
+      for (int pp = tid; pp < n_pos; pp += kThreads) {
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          const T tau = safety / (qmax[q] + L[q]);
+          const T a = one / (one + tau * p.q_i[sample(q) * n_pos + pp]);
+          av[(size_t)pp * S + q] = a;
+          dv[(size_t)pp * S + q] = tau * a;
+        }
+      }
+    }
+  }
+
+  // ---- initial state: y = ybar = y0 (the target), lambda = dual0 -----------
   for (int pp = tid; pp < n_pos; pp += kThreads) {
     T t[S];
 #pragma unroll
-    for (int q = 0; q < S; ++q) t[q] = p.tgt_i[sample(q) * n_pos + pp];
+    for (int q = 0; q < S; ++q) {
+      if constexpr (kQP) t[q] = p.y0_i ? p.y0_i[sample(q) * n_pos + pp] : zero;
+      else t[q] = p.tgt_i[sample(q) * n_pos + pp];
+    }
     store_pack<T, S>(y + (size_t)pp * S, t);
     store_pack<T, S>(ybar + (size_t)pp * S, t);
   }
@@ -389,8 +460,9 @@ cp_forward_kernel(const FwdParams<T> p) {
     y[(size_t)n_pos * S + q] = zero;
     ybar[(size_t)n_pos * S + q] = zero;
     lam[(size_t)m_pos * S + q] = zero;
-    const T tau = p.accelerated ? safety / L[q] : safety / (one + L[q]);
+    const T tau = (p.accelerated && qmin[q] > zero) ? safety / L[q] : safety / (qmax[q] + L[q]);
     sc.tau[q] = tau;
+    sc.gam[q] = qmin[q];
     sc.sigma[q] = safety / L[q];
     sc.theta[q] = one;
     sc.a[q] = one / (one + tau * one);
@@ -454,22 +526,29 @@ cp_forward_kernel(const FwdParams<T> p) {
   // violation and the primal and dual objectives of y+.
   auto phase_b = [&](auto full_c, int act, int& fin) {
     constexpr bool kFull = decltype(full_c)::value;
-    T stm[S], resm[S], ps[S], ds[S], a_s[S], d_s[S], theta_s[S];
+    T stm[S], resm[S], ps[S], ds[S], a_s[S], d_s[S], theta_s[S], tau_s[S];
 #pragma unroll
     for (int q = 0; q < S; ++q) {
       stm[q] = resm[q] = ps[q] = ds[q] = zero;
       a_s[q] = sc.a[q];  // per-sample scalars of this iteration, read once
       d_s[q] = sc.d[q];
       theta_s[q] = sc.theta[q];
+      tau_s[q] = sc.tau[q];
     }
     for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
       const int j = cols.line(sl, lane);
       const int pp = sl * kC + lane;
-      T tg[S], lb[S], ub[S];
+      T tg[S], lb[S], ub[S], qv[S];
 #pragma unroll
       for (int q = 0; q < S; ++q) {
         const int64_t b = sample(q);
-        tg[q] = p.tgt_i[b * n_pos + pp];
+        if constexpr (kQP) {
+          tg[q] = p.c_i[b * n_pos + pp];
+          qv[q] = p.q_i[b * n_pos + pp];
+        } else {
+          tg[q] = p.tgt_i[b * n_pos + pp];
+          qv[q] = one;
+        }
         lb[q] = p.lo_i[b * p.bstride_i + pp];
         ub[q] = p.up_i[b * p.bstride_i + pp];
       }
@@ -484,9 +563,17 @@ cp_forward_kernel(const FwdParams<T> p) {
           if (!((act >> q) & 1)) continue;
           const size_t js = (size_t)pp * S + q;
           const T yo = yv[q];
-          const T c = -tg[q];
-          const T aa = p.diag ? av[js] : a_s[q];
-          const T dd = p.diag ? dv[js] : d_s[q];
+          const T c = kQP ? tg[q] : -tg[q];
+          const T qj = qv[q];
+          T aa, dd;
+          if (kQP && p.accelerated) {
+            // Accelerated steps change tau: proximal_coefficients every iteration.
+            aa = one / (one + tau_s[q] * qj);
+            dd = tau_s[q] * aa;
+          } else {
+            aa = pv ? av[js] : a_s[q];
+            dd = pv ? dv[js] : d_s[q];
+          }
           const T off = (-dd) * c;
           const T yr = (aa * yo - dd * t[q]) + off;
           const T l = lb[q];
@@ -497,12 +584,12 @@ cp_forward_kernel(const FwdParams<T> p) {
           if (!finite(yn)) fin &= ~(1 << q);
           if constexpr (kFull) {
             resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
-            ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
+            ps[q] = ps[q] + ((T(0.5) * qj * yn) * yn + c * yn);
             const T tt = c + t[q];
-            const T mn = clip(-tt / one, l, u);
-            ds[q] = ds[q] + (T(0.5) * one * (mn * mn) + tt * mn);
+            const T mn = dual_minimiser<kQP>(tt, qj, l, u);
+            ds[q] = ds[q] + (T(0.5) * qj * (mn * mn) + tt * mn);
           }
-          const T inner = (one * yn + c) + t[q];
+          const T inner = (qj * yn + c) + t[q];
           stm[q] = pmax(stm[q], fabs(yn - clip(yn - inner, l, u)));
         }
         store_pack<T, S>(y + (size_t)pp * S, yv);
@@ -588,11 +675,17 @@ cp_forward_kernel(const FwdParams<T> p) {
       for (int sl = warp; sl < sv.nsl_c; sl += kWarps) {
         const int j = cols.line(sl, lane);
         const int pp = sl * kC + lane;
-        T tg[S], lb[S], ub[S];
+        T tg[S], lb[S], ub[S], qv[S];
 #pragma unroll
         for (int q = 0; q < S; ++q) {
           const int64_t b = sample(q);
-          tg[q] = p.tgt_i[b * n_pos + pp];
+          if constexpr (kQP) {
+            tg[q] = p.c_i[b * n_pos + pp];
+            qv[q] = p.q_i[b * n_pos + pp];
+          } else {
+            tg[q] = p.tgt_i[b * n_pos + pp];
+            qv[q] = one;
+          }
           lb[q] = p.lo_i[b * p.bstride_i + pp];
           ub[q] = p.up_i[b * p.bstride_i + pp];
         }
@@ -605,14 +698,15 @@ cp_forward_kernel(const FwdParams<T> p) {
           for (int q = 0; q < S; ++q) {
             if (!((act >> q) & 1)) continue;
             const T yn = yv[q];
-            const T c = -tg[q];
+            const T c = kQP ? tg[q] : -tg[q];
+            const T qj = qv[q];
             const T l = lb[q];
             const T u = ub[q];
             resm[q] = pmax(resm[q], pmax(pmax(l - yn, zero), pmax(yn - u, zero)));
-            ps[q] = ps[q] + ((T(0.5) * one * yn) * yn + c * yn);
+            ps[q] = ps[q] + ((T(0.5) * qj * yn) * yn + c * yn);
             const T tt = c + t[q];
-            const T mn = clip(-tt / one, l, u);
-            ds[q] = ds[q] + (T(0.5) * one * (mn * mn) + tt * mn);
+            const T mn = dual_minimiser<kQP>(tt, qj, l, u);
+            ds[q] = ds[q] + (T(0.5) * qj * (mn * mn) + tt * mn);
           }
         }
       }
@@ -694,7 +788,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       }
       if (p.accelerated) {
         const T tau = sc.tau[q];
-        const T nt = one / sqrt(one + one * tau);
+        const T nt = one / sqrt(one + sc.gam[q] * tau);
         const T ntau = nt * tau;
         sc.tau[q] = ntau;
         sc.sigma[q] = sc.sigma[q] / nt;
@@ -723,7 +817,7 @@ cp_forward_kernel(const FwdParams<T> p) {
       p.it_out[b] = sc.count[q];
       p.res_out[b] = sc.res_out[q];
       p.gap_out[b] = sc.gap_out[q];
-      const bool feas = p.feasible ? (p.feasible[b] != 0) : true;
+      const bool feas = (p.feasible ? (p.feasible[b] != 0) : true) && (!kQP || sc.valid[q]);
       p.conv_out[b] = (sc.conv[q] && feas) ? 1 : 0;
     }
   }
@@ -752,18 +846,18 @@ __global__ void arrange_values_kernel(const T* values, const int* slot, int coun
   }
 }
 
-template <typename T, int S, int NT, bool kShared>
+template <typename T, int S, int NT, bool kShared, bool kQP>
 cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaStream_t stream) {
   const unsigned grid = (unsigned)((p.batch + S - 1) / S);
   if (smem) {
-    auto kern = cp_forward_kernel<T, S, NT, true, kShared>;
+    auto kern = cp_forward_kernel<T, S, NT, true, kShared, kQP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem_bytes);
     if (e != cudaSuccess) return e;
     kern<<<grid, NT, smem_bytes, stream>>>(p);
   } else {
     if constexpr (NT == kForwardThreads) {
-      cp_forward_kernel<T, S, NT, false, kShared><<<grid, NT, 0, stream>>>(p);
+      cp_forward_kernel<T, S, NT, false, kShared, kQP><<<grid, NT, 0, stream>>>(p);
     } else {
       return cudaErrorInvalidValue;
     }
@@ -773,28 +867,34 @@ cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaSt
 
 // Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads, and S = 1
 // with 2 or 4 times as many threads for shared-memory tiles of one sample.
-template <typename T, bool kShared>
+// The diagonal QP is built for the one-sample shapes only.
+template <typename T, bool kShared, bool kQP>
 cudaError_t launch_shared(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                           cudaStream_t stream) {
   if (NT == 2 * kForwardThreads)
-    return S == 1 ? launch_s<T, 1, 2 * kForwardThreads, kShared>(p, smem, smem_bytes, stream)
+    return S == 1 ? launch_s<T, 1, 2 * kForwardThreads, kShared, kQP>(p, smem, smem_bytes, stream)
                   : cudaErrorInvalidValue;
   if (NT == kWideThreads)
-    return S == 1 ? launch_s<T, 1, kWideThreads, kShared>(p, smem, smem_bytes, stream)
+    return S == 1 ? launch_s<T, 1, kWideThreads, kShared, kQP>(p, smem, smem_bytes, stream)
                   : cudaErrorInvalidValue;
   if (NT != kForwardThreads) return cudaErrorInvalidValue;
-  switch (S) {
-    case 1: return launch_s<T, 1, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
-    case 2: return launch_s<T, 2, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
-    case 4: return launch_s<T, 4, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
-    case 8: return launch_s<T, 8, kForwardThreads, kShared>(p, smem, smem_bytes, stream);
-    default: return cudaErrorInvalidValue;
+  if constexpr (kQP) {
+    return S == 1 ? launch_s<T, 1, kForwardThreads, kShared, true>(p, smem, smem_bytes, stream)
+                  : cudaErrorInvalidValue;
+  } else {
+    switch (S) {
+      case 1: return launch_s<T, 1, kForwardThreads, kShared, false>(p, smem, smem_bytes, stream);
+      case 2: return launch_s<T, 2, kForwardThreads, kShared, false>(p, smem, smem_bytes, stream);
+      case 4: return launch_s<T, 4, kForwardThreads, kShared, false>(p, smem, smem_bytes, stream);
+      case 8: return launch_s<T, 8, kForwardThreads, kShared, false>(p, smem, smem_bytes, stream);
+      default: return cudaErrorInvalidValue;
+    }
   }
 }
 
-template <typename T, int S, int NT, bool kShared>
+template <typename T, int S, int NT, bool kShared, bool kQP>
 int blocks_per_sm_s(size_t smem_bytes) {
-  auto kern = cp_forward_kernel<T, S, NT, true, kShared>;
+  auto kern = cp_forward_kernel<T, S, NT, true, kShared, kQP>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes) !=
       cudaSuccess)
     return 0;
@@ -804,27 +904,35 @@ int blocks_per_sm_s(size_t smem_bytes) {
   return per_sm;
 }
 
-template <typename T, bool kShared>
+template <typename T, bool kShared, bool kQP>
 int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
   if (NT == 2 * kForwardThreads)
-    return S == 1 ? blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared>(smem_bytes) : 0;
-  if (NT == kWideThreads) return S == 1 ? blocks_per_sm_s<T, 1, kWideThreads, kShared>(smem_bytes) : 0;
+    return S == 1 ? blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared, kQP>(smem_bytes) : 0;
+  if (NT == kWideThreads)
+    return S == 1 ? blocks_per_sm_s<T, 1, kWideThreads, kShared, kQP>(smem_bytes) : 0;
   if (NT != kForwardThreads) return 0;
-  switch (S) {
-    case 1: return blocks_per_sm_s<T, 1, kForwardThreads, kShared>(smem_bytes);
-    case 2: return blocks_per_sm_s<T, 2, kForwardThreads, kShared>(smem_bytes);
-    case 4: return blocks_per_sm_s<T, 4, kForwardThreads, kShared>(smem_bytes);
-    case 8: return blocks_per_sm_s<T, 8, kForwardThreads, kShared>(smem_bytes);
-    default: return 0;
+  if constexpr (kQP) {
+    return S == 1 ? blocks_per_sm_s<T, 1, kForwardThreads, kShared, true>(smem_bytes) : 0;
+  } else {
+    switch (S) {
+      case 1: return blocks_per_sm_s<T, 1, kForwardThreads, kShared, false>(smem_bytes);
+      case 2: return blocks_per_sm_s<T, 2, kForwardThreads, kShared, false>(smem_bytes);
+      case 4: return blocks_per_sm_s<T, 4, kForwardThreads, kShared, false>(smem_bytes);
+      case 8: return blocks_per_sm_s<T, 8, kForwardThreads, kShared, false>(smem_bytes);
+      default: return 0;
+    }
   }
 }
 
 }  // namespace
 
 template <typename T>
-int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes) {
-  return shared_values ? blocks_per_sm_shared<T, true>(S, NT, smem_bytes)
-                       : blocks_per_sm_shared<T, false>(S, NT, smem_bytes);
+int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, bool qp) {
+  if (qp)
+    return shared_values ? blocks_per_sm_shared<T, true, true>(S, NT, smem_bytes)
+                         : blocks_per_sm_shared<T, false, true>(S, NT, smem_bytes);
+  return shared_values ? blocks_per_sm_shared<T, true, false>(S, NT, smem_bytes)
+                       : blocks_per_sm_shared<T, false, false>(S, NT, smem_bytes);
 }
 
 template <typename T>
@@ -863,16 +971,19 @@ cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int 
 template <typename T>
 cudaError_t launch_forward(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                            cudaStream_t stream) {
-  return p.vr ? launch_shared<T, true>(p, S, NT, smem, smem_bytes, stream)
-              : launch_shared<T, false>(p, S, NT, smem, smem_bytes, stream);
+  if (p.q_i)
+    return p.vr ? launch_shared<T, true, true>(p, S, NT, smem, smem_bytes, stream)
+                : launch_shared<T, false, true>(p, S, NT, smem, smem_bytes, stream);
+  return p.vr ? launch_shared<T, true, false>(p, S, NT, smem, smem_bytes, stream)
+              : launch_shared<T, false, false>(p, S, NT, smem, smem_bytes, stream);
 }
 
 template cudaError_t launch_forward<double>(const FwdParams<double>&, int, int, bool, size_t,
                                             cudaStream_t);
 template cudaError_t launch_forward<float>(const FwdParams<float>&, int, int, bool, size_t,
                                            cudaStream_t);
-template int forward_blocks_per_sm<double>(int, int, bool, size_t);
-template int forward_blocks_per_sm<float>(int, int, bool, size_t);
+template int forward_blocks_per_sm<double>(int, int, bool, size_t, bool);
+template int forward_blocks_per_sm<float>(int, int, bool, size_t, bool);
 template size_t forward_static_smem<double>(int, int);
 template size_t forward_static_smem<float>(int, int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);

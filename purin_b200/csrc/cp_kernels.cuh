@@ -51,6 +51,12 @@ struct FwdParams {
   const T* lo_i;     // (B or 1, n_pos)
   const T* up_i;
   int64_t bstride_i;  // 0 (shared bounds) or n_pos
+  // General diagonal QP (null for the distance projection, where q = 1,
+  // c = -target and y0 = target): per-sample q, c and y0 in the internal
+  // column order, (B, n_pos) each; y0_i null means zeros.
+  const T* q_i;
+  const T* c_i;
+  const T* y0_i;
 };
 
 template <typename T>
@@ -78,6 +84,16 @@ struct AdjParams {
   int32_t* lin_status;
   T* lin_residual;
   int32_t* device_error;
+  // General diagonal QP (qp = 1; diagonal_qp.py:133-222): per-sample q and c
+  // replace q = 1, c = -target; the dual cotangent enters the right-hand
+  // side; q and c get cotangents.
+  int qp;
+  const T* q;         // (B, n)
+  const T* c;         // (B, n)
+  const T* cot_dual;  // (B, m) or null
+  T* g_q;             // (B, n) or null
+  T* g_c;             // (B, n) or null
+  int norm_bound;     // QP backward only: L from |K| row/column sums
   // configuration
   int accelerated;
   int diag;
@@ -102,7 +118,8 @@ struct AdjParams {
   uint8_t* ycode;  // B * n
   uint8_t* dcode;  // B * m
   T* steps;        // B * 2 : tau, sigma
-  T* dsteps;       // B * (2n + m) : a, d (per column), sigma (per row); diagonal steps only
+  T* dsteps;       // B * (2n + m) : a, d (per column), sigma (per row); diagonal steps or QP
+                   // (QP: B * (3n + m), tau per column after sigma)
   T* thresh;       // B
   T* resinf;       // B
   T* basis;        // grid * (R + 1) * W
@@ -154,7 +171,7 @@ size_t forward_static_smem(int S, int NT);
 // Resident CTAs per SM of the shared-memory forward kernel (0 when the
 // occupancy query fails).
 template <typename T>
-int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes);
+int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, bool qp = false);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
 // dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0 for b < rows.

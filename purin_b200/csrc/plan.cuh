@@ -64,6 +64,10 @@ struct PurinCpPlan {
   void* sell_block = nullptr;
   // Resident forward CTAs per SM by [diagonal steps][shared values][tile shape]
   // (-1: not queried yet); filled on first use, the same value by any thread.
-  int fwd_blocks[2][2][8] = {{{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
+  // [distance | distance + diagonal steps | QP | QP with per-variable coefficients]
+  // x [per-sample values | shared values] x tile shape
+  int fwd_blocks[4][2][8] = {{{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
+                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
+                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
                              {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}}};
 };
