@@ -84,6 +84,9 @@ def parse_args():
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
                         "a loose value such as 1e-3 lets samples converge so that the VJP "
                         "runs full GMRES solves instead of being gated to zero")
+    p.add_argument("--problem", default="projection", choices=["projection", "qp"],
+                   help="qp: configuration 2's structure as a general diagonal QP "
+                        "(PreparedDiagonalQP), fwd + VJP w.r.t. q, c, values, rhs and bounds")
     return p.parse_args()
 
 
@@ -237,6 +240,183 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+QP_METRIC = "QP samples/sec at fixed iters (fwd+VJP)"
+
+
+def cpu_baseline_qp(samples):
+    """The NumPy diagonal-QP oracle (fwd 2000 iterations + VJP) on a bounded sample."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from helpers import oracle_config  # noqa: E402  (test infrastructure, checker only)
+    from oracle.diagonal_qp import OracleDiagonalQP  # noqa: E402
+    from purin_b200 import ChambollePockConfig
+    from purin_b200.workloads import qp_workload
+
+    structure, q, c, values, rhs, lower, upper, targets = qp_workload(samples)
+    qp = OracleDiagonalQP(structure.variable_size, structure.equality_rows,
+                          structure.inequality_rows,
+                          oracle_config(ChambollePockConfig(max_iterations=2000)))
+    b = q.shape[0]
+    data = (q, c, np.broadcast_to(values, (b,) + values.shape[1:]), rhs,
+            np.broadcast_to(lower, q.shape), np.broadcast_to(upper, q.shape))
+    t0 = time.perf_counter()
+    result, saved = qp.solve(data)
+    qp.vjp(saved["out"], saved["data"], result["y"] - targets)
+    elapsed = time.perf_counter() - t0
+    return {"value": samples / elapsed, "unit": "samples/s", "cores": 1, "kind": "port",
+            "sample": f"{samples} samples of the QP workload (fwd 2000 it + VJP) in "
+                      f"{elapsed:.1f} s: the NumPy diagonal-QP restatement (oracle/)"}
+
+
+def main_qp(args, world, rank, local_rank, device, barrier):
+    """``--problem qp``: configuration 2's structure as a PreparedDiagonalQP."""
+    import torch
+    import torch.distributed as dist
+
+    from purin_b200 import ChambollePockConfig
+    from purin_b200.diagonal_qp import QPData
+    from purin_b200.workloads import qp_workload
+
+    batch = args.batch or DEFAULT_BATCH[CONFIG_INDEX]
+    total = batch * world
+    structure, q, c, values, rhs, lower, upper, targets = qp_workload(batch, seed=rank)
+    cfg = ChambollePockConfig(max_iterations=2000)
+    if args.cp_tolerance is not None:
+        cfg = dataclasses.replace(cfg, tolerance=args.cp_tolerance)
+    solver = structure.prepare(batch_size=batch, config=cfg, dtype=torch.float64,
+                               backend=str(device))
+    solver.set_shard(rank * batch, total)
+    n, m = q.shape[1], rhs.shape[1]
+    dev = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device=device)
+    q_d, c_d, rhs_d, t_d = dev(q), dev(c), dev(rhs), dev(targets)
+    vals_d, lo_d, up_d = dev(values), dev(lower)[None], dev(upper)[None]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step(q_, c_, rhs_, t_):
+        # The constraint matrix and the bounds are shared by the batch (stride-0 views).
+        leaves = [x.detach().requires_grad_(True) for x in (q_, c_, vals_d, rhs_, lo_d, up_d)]
+        data = QPData(leaves[0], leaves[1], leaves[2].expand(batch, -1, -1), leaves[3],
+                      leaves[4].expand(batch, -1), leaves[5].expand(batch, -1))
+        res = solver.solve(data)
+        loss = 0.5 * ((res.y - t_) ** 2).sum()
+        loss.backward()
+        return loss, leaves
+
+    for _ in range(args.warmup):
+        step(q_d, c_d, rhs_d, t_d)
+    barrier()
+    timers, step_ms = [], []
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            solver.record_launches(timers)
+            start.record()
+            step(q_d, c_d, rhs_d, t_d)
+            end.record()
+            solver.record_launches(None)
+            torch.cuda.synchronize(device)
+            step_ms.append(start.elapsed_time(end))
+        barrier()
+    clock_info = clocks.summary()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(float(sum(step_ms) / len(step_ms)))
+    per_kernel = {}
+    for name, s0, e0 in timers:
+        per_kernel.setdefault(name, []).append(s0.elapsed_time(e0))
+    per_step = lambda name: (sum(per_kernel[name]) / args.steps if name in per_kernel
+                             else float("nan"))
+    fwd_ms, adj_ms = per_step("forward"), per_step("adjoint")
+    launches = count_native_launches(lambda: step(q_d, c_d, rhs_d, t_d), device) * args.steps
+    with torch.no_grad():
+        res = solver.solve(QPData(q_d, c_d, vals_d.expand(batch, -1, -1), rhs_d,
+                                  lo_d.expand(batch, -1), up_d.expand(batch, -1)))
+    iters_total = int(res.iterations.sum().item())
+    eligible = int(res.gradient_eligible.sum().item())
+    # (6n + 3m) * 8 B per sample-iteration: read y, ybar, q, c, lambda, rhs; write
+    # y, ybar, lambda (the shared constraint values are amortised, counted 0).
+    fwd_bytes = float(iters_total) * (6 * n + 3 * m) * 8
+    hbm, peak_kind = peaks()
+    achieved = fwd_bytes / (fwd_ms / 1000.0) / 1e9
+
+    # End to end: q, c, rhs and targets from pinned host memory; loss and the
+    # gradients w.r.t. q, c and rhs back to pinned host memory.
+    pin = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64).pin_memory()
+    q_h, c_h, rhs_h, t_h = pin(q), pin(c), pin(rhs), pin(targets)
+    gq_h, gc_h, grhs_h = (torch.empty_like(x).pin_memory() for x in (q_h, c_h, rhs_h))
+    loss_h = torch.empty((), dtype=torch.float64).pin_memory()
+
+    def step_e2e():
+        to = lambda x: x.to(device, non_blocking=True)
+        loss, leaves = step(to(q_h), to(c_h), to(rhs_h), to(t_h))
+        gq_h.copy_(leaves[0].grad, non_blocking=True)
+        gc_h.copy_(leaves[1].grad, non_blocking=True)
+        grhs_h.copy_(leaves[3].grad, non_blocking=True)
+        loss_h.copy_(loss.detach(), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    barrier()
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        step_e2e()
+        end.record()
+        torch.cuda.synchronize(device)
+        e2e_ms.append(start.elapsed_time(end))
+    barrier()
+    e2e = max_over_ranks(float(sum(e2e_ms) / len(e2e_ms)))
+    h2d = (q_h.numel() + c_h.numel() + rhs_h.numel() + t_h.numel()) * 8
+    d2h = (gq_h.numel() + gc_h.numel() + grhs_h.numel() + 1) * 8
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_qp(args.cpu_samples or 8)
+    if rank == 0:
+        line = {
+            "metric": QP_METRIC, "value": total / (ms / 1000.0), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (configuration 2's seeded structure as a diagonal QP; no dataset)",
+            "config": {
+                "workload": "qp: PreparedDiagonalQP, fp64, n=2048, me=512, mi=1024, 8 nnz/row "
+                            "(values shared by the batch), per-sample q~U(0.5,2), c=-q*candidate, "
+                            "rhs; bounds shared; 2000 fixed-step CP iterations (tolerance "
+                            f"{cfg.tolerance:g} stopping test kept); loss 0.5||y-t||^2, "
+                            "gradients w.r.t. q, c, values, rhs, lower, upper",
+                "samples_per_gpu": batch, "global_batch": total,
+                "l2": "flushed between timed steps (256 MB write outside the step events)",
+                "gradient_eligible": f"{eligible}/{batch} on rank 0",
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "cp_forward_kernel<kQP>", "achieved": achieved,
+                "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                "peak_source": peak_kind, "algorithmic_bytes_per_launch": fwd_bytes,
+                "launch_ms": fwd_ms,
+                "note": "(6n+3m)*8 B per sample-iteration x executed iterations",
+            },
+            "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms},
+            "gpu_launches": launches,
+            "e2e": {"value": total / (e2e / 1000.0), "unit": "samples/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e},
+            "clocks": clock_info,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -264,6 +444,10 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
+
+    if args.problem == "qp":
+        main_qp(args, world, rank, local_rank, device, barrier)
+        return
 
     index = args.config
     vjp = (args.mode or ("fwd+vjp" if index == CONFIG_INDEX else "fwd")) == "fwd+vjp"

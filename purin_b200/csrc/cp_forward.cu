@@ -194,6 +194,28 @@ __device__ __forceinline__ void tile_reduce(T (&v)[S], T (&scratch)[kWarps][S]) 
   }
 }
 
+// Per-sample tile maximum of values of any sign (tile_reduce's max starts from
+// zero, which suits its nonnegative quantities only).
+template <typename T, int S, int kWarps>
+__device__ __forceinline__ void tile_max_signed(T (&v)[S], T (&scratch)[kWarps][S]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < S; ++q) v[q] = warp_max32(v[q]);
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < S; ++q) scratch[warp][q] = v[q];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < S; ++q) {
+    T total = scratch[0][q];
+#pragma unroll 8
+    for (int w = 1; w < kWarps; ++w) total = pmax(total, scratch[w][q]);
+    v[q] = total;
+  }
+}
+
 template <typename T, int S>
 __device__ __forceinline__ void store_pack(T* p, const T (&v)[S]) {
   if constexpr (sizeof(T) * S % 16 == 0) {
@@ -415,8 +437,8 @@ cp_forward_kernel(const FwdParams<T> p) {
         if (!(p.lo_i[b * p.bstride_i + pp] <= p.up_i[b * p.bstride_i + pp])) bad[q] = one;
       }
     }
-    tile_reduce<T, S, true>(nmin, sc.s_red);
-    tile_reduce<T, S, true>(qmax, sc.s_red);
+    tile_max_signed<T, S>(nmin, sc.s_red);
+    tile_max_signed<T, S>(qmax, sc.s_red);
     tile_reduce<T, S, true>(bad, sc.s_red);
 #pragma unroll
     for (int q = 0; q < S; ++q) {

@@ -17,6 +17,7 @@ Differences: arrays are torch tensors on a CUDA device (``backend``), and
 
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass
 from typing import NamedTuple
 
@@ -101,12 +102,16 @@ class _QPSolve(torch.autograd.Function):
         converged = torch.empty((batch,), dtype=torch.uint8, device=dev)
         ws_bytes = layer._plan.workspace_size(_native.QP_OP_FORWARD, batch, layer._cfg)
         ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        # One row of values for the whole batch (a broadcast constraint matrix) is
+        # passed with stride 0; otherwise one row per sample.
+        stride = 0 if values.shape[0] == 1 and batch != 1 else values.shape[1]
         args = _native.QpForwardArgs(
-            batch, _ptr(q), _ptr(c), _ptr(values), values.shape[1], _ptr(rhs), _ptr(lower),
+            batch, _ptr(q), _ptr(c), _ptr(values), stride, _ptr(rhs), _ptr(lower),
             _ptr(upper), n, _ptr(y0), _ptr(dual0), _ptr(tolerance), layer._sample_offset,
             layer._total_batch, _ptr(y), _ptr(dual), _ptr(iterations), _ptr(residual), _ptr(gap),
             _ptr(converged))
-        layer._plan.qp_forward(layer._cfg, args, ws.data_ptr(), ws_bytes, layer._stream())
+        with layer._timed("forward"):
+            layer._plan.qp_forward(layer._cfg, args, ws.data_ptr(), ws_bytes, layer._stream())
         ctx.layer = layer
         ctx.save_for_backward(q, c, values, rhs, lower, upper, y, dual, converged)
         ctx.mark_non_differentiable(iterations, residual, gap, converged)
@@ -125,7 +130,8 @@ class _QPSolve(torch.autograd.Function):
         if layer.differentiate_duals and gdual is not None and m > 0:
             cot_dual = gdual.contiguous()
         out = lambda k, shape: torch.empty(shape, dtype=dt, device=dev) if need[k] else None
-        grads = (out(0, (batch, n)), out(1, (batch, n)), out(2, tuple(values.shape)),
+        shared = values.shape[0] == 1 and batch != 1
+        grads = (out(0, (batch, n)), out(1, (batch, n)), out(2, (batch, values.shape[1])),
                  out(3, (batch, m)), out(4, (batch, n)), out(5, (batch, n)))
         status = torch.empty((batch,), dtype=torch.int32, device=dev)
         lres = torch.empty((batch,), dtype=dt, device=dev)
@@ -134,17 +140,21 @@ class _QPSolve(torch.autograd.Function):
         ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
         g_q, g_c, g_values, g_rhs, g_lower, g_upper = grads
         args = _native.QpAdjointArgs(
-            batch, _ptr(q), _ptr(c), _ptr(values), values.shape[1], _ptr(rhs), _ptr(lower),
+            batch, _ptr(q), _ptr(c), _ptr(values), 0 if shared else values.shape[1], _ptr(rhs),
+            _ptr(lower),
             _ptr(upper), n, _ptr(y), _ptr(dual), _ptr(converged), _ptr(gy), _ptr(cot_dual),
             layer._sample_offset, layer._total_batch, _ptr(g_q), _ptr(g_c), _ptr(g_values),
             _ptr(g_rhs), _ptr(g_lower), _ptr(g_upper), _ptr(status), _ptr(lres), _ptr(err))
-        layer._plan.qp_adjoint(layer._cfg, layer._lin, args, ws.data_ptr(), ws_bytes,
-                               layer._stream())
+        with layer._timed("adjoint"):
+            layer._plan.qp_adjoint(layer._cfg, layer._lin, args, ws.data_ptr(), ws_bytes,
+                                   layer._stream())
         object.__setattr__(layer, "_last_linear", (status, lres))
         if int(err.item()) != 0:
             raise RuntimeError("purin_qp_adjoint: a bounded device wait timed out; "
                                "gradients are invalid")
-        return (*grads, None, None, None, None)
+        if shared and g_values is not None:
+            g_values = g_values.sum(dim=0, keepdim=True)
+        return (g_q, g_c, g_values, g_rhs, g_lower, g_upper, None, None, None, None)
 
 
 @dataclass(frozen=True, eq=False)
@@ -211,6 +221,7 @@ class PreparedDiagonalQP:
                                           float(cfg.implicit_gradient.adjoint_tolerance)))
         set_("_sample_offset", 0)
         set_("_total_batch", int(self.batch_size))
+        set_("_timers", None)
 
     @property
     def support(self):
@@ -227,6 +238,24 @@ class PreparedDiagonalQP:
 
     def _stream(self):
         return ctypes_stream(torch.cuda.current_stream(self._device))
+
+    def record_launches(self, timers: list | None):
+        """Collect (kernel, start_event, end_event) for every native launch, or stop (None)."""
+        object.__setattr__(self, "_timers", timers)
+
+    @contextlib.contextmanager
+    def _timed(self, name):
+        timers = self._timers
+        if timers is None:
+            yield
+            return
+        stream = torch.cuda.current_stream(self._device)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        yield
+        end.record(stream)
+        timers.append((name, start, end))
 
     # -- ordered sparse products (the reference's accumulation order) -------------
     def _matvec(self, values, x):
@@ -280,14 +309,20 @@ class PreparedDiagonalQP:
                  else torch.as_tensor(initial_dual, dtype=dt, device=dev))
         if tuple(y0.shape) != (b, n) or tuple(dual0.shape) != (b, m):
             raise ValueError("initial primal/dual shapes do not match the prepared QP")
-        scale = self._row_scale(data.values)
-        scaled_values = data.values * scale[:, :, None]
+        # A constraint matrix broadcast over the batch (stride 0, as dense_qp_data
+        # builds it) is scaled and handed to the kernels once for all samples.
+        shared = b > 1 and data.values.stride(0) == 0
+        values = data.values[:1] if shared else data.values
+        scale = self._row_scale(values)
+        scaled_values = values * scale[:, :, None]
+        if shared:
+            scale = scale.expand(b, m)
         scaled_rhs = data.rhs * scale
         one = torch.ones((), dtype=dt, device=dev)
         min_scale = (torch.minimum(one, scale.min(dim=1).values) if m > 0
                      else torch.ones((b,), dtype=dt, device=dev))
         tolerance = (self.config.tolerance * torch.minimum(one, min_scale)).detach()
-        values_csr = scaled_values.reshape(b, m * width)[:, self._positions]
+        values_csr = scaled_values.reshape(scaled_values.shape[0], m * width)[:, self._positions]
         y, dual, iterations, _, _, cp_converged = _QPSolve.apply(
             data.q.contiguous(), data.c.contiguous(), values_csr.contiguous(),
             scaled_rhs.contiguous(), data.lower.contiguous(), data.upper.contiguous(),

@@ -169,3 +169,36 @@ def make_workload(index: int, batch: int | None = None, *, dtype: str | None = N
         cfg = ChambollePockConfig(accelerated=True, max_iterations=1000)
         return Workload("config4", problem, theta, cand, cfg, dtype or "float32", weights=weights)
     raise ValueError("configuration index must be 0..4")
+
+
+def qp_workload(batch: int, *, seed: int = 0):
+    """Configuration 2's structure as a general diagonal QP (PreparedDiagonalQP).
+
+    The same seeded rows (512 equality, 1024 inequality, 8 nnz per row over
+    n = 2048 variables, values N(0,1), shared by the batch), per-variable
+    bounds l ~ U(-2,-0.5), u ~ U(0.5,2) and per-sample right-hand sides from a
+    seeded x0 as in configuration 2; per sample q ~ U(0.5, 2)^n and
+    c = -q * candidate (a q-weighted projection of the candidate 2 N(0,1)), and
+    a loss target t ~ N(0,1)^n.  Returns (structure, q, c, values (1, m, 8),
+    rhs, lower (n,), upper (n,), targets) as NumPy arrays.
+    """
+    from purin_b200.diagonal_qp import QPStructure
+
+    n, me, mi, k = 2048, 512, 1024, 8
+    rng = np.random.default_rng(seed)
+    A_eq = _random_rows(rng, me, n, k)
+    A_in = _random_rows(rng, mi, n, k)
+    lower = rng.uniform(-2.0, -0.5, n)
+    upper = rng.uniform(0.5, 2.0, n)
+    x0 = rng.uniform(-0.5, 0.5, (batch, n))
+    slack = rng.uniform(0.0, 0.1, (batch, mi))
+    candidates = 2.0 * rng.normal(size=(batch, n))
+    rhs = np.concatenate([(A_eq @ x0.T).T, (A_in @ x0.T).T + slack], axis=1)
+    q = rng.uniform(0.5, 2.0, (batch, n))
+    c = -q * candidates
+    targets = rng.normal(size=(batch, n))
+    rows = [tuple(int(j) for j in A.indices[A.indptr[i]:A.indptr[i + 1]])
+            for A in (A_eq, A_in) for i in range(A.shape[0])]
+    structure = QPStructure(n, tuple(rows[:me]), tuple(rows[me:]))
+    values = np.concatenate([A_eq.data, A_in.data]).reshape(1, me + mi, k)
+    return structure, q, c, values, rhs, lower, upper, targets
