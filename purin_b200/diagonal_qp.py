@@ -272,6 +272,8 @@ class PreparedDiagonalQP:
         flat = values.reshape(values.shape[0], -1)
         out = torch.zeros((y.shape[0], self.structure.variable_size), dtype=y.dtype,
                           device=y.device)
+        if values.shape[1] == 0:  # no constraint rows: K.T y = 0
+            return out
         zero = torch.zeros((), dtype=y.dtype, device=y.device)
         for d in range(self._col_pos.shape[1]):
             term = flat[:, self._col_pos[:, d]] * y[:, self._col_row[:, d]]

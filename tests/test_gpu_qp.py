@@ -167,3 +167,56 @@ def test_broadcast_constraint_matrix_matches_per_sample_values():
     np.testing.assert_allclose(ga.cpu().numpy(), gb.cpu().numpy(), rtol=1e-12, atol=1e-14)
     for k in (0, 1, 3, 4, 5):
         np.testing.assert_array_equal(ta[k].cpu().numpy(), tb[k].cpu().numpy())
+
+
+def _box_case(B=4, n=6, bad_sample=None):
+    rng = np.random.default_rng(5)
+    q = rng.uniform(0.5, 2, (B, n))
+    c = rng.normal(size=(B, n))
+    lower = np.full((B, n), -0.7)
+    upper = np.full((B, n), 0.9)
+    if bad_sample is not None:
+        lower[bad_sample, 2] = 1.5  # lower > upper: the sample is not a valid QP
+    return (q, c, np.zeros((B, 0, 1)), np.zeros((B, 0)), lower, upper)
+
+
+@pytest.mark.parametrize("bad_sample", [None, 1])
+def test_box_only_qp(bad_sample):
+    """No constraint rows: y = clip(-c/q, l, u) with dy/dc = -1/q off the bounds, 0 on
+    them; a sample with lower > upper is reported unconverged with zero gradients
+    (diagonal_qp.py:120-123), as the oracle does."""
+    data = _box_case(bad_sample=bad_sample)
+    cfg = ChambollePockConfig(max_iterations=5000, tolerance=1e-12)
+    oracle = OracleDiagonalQP(6, (), (), oracle_config(cfg))
+    want, _ = oracle.solve(data)
+    solver = QPStructure(6).prepare(batch_size=4, config=cfg)
+    tensors = [torch.as_tensor(a, device=DEV).requires_grad_(True) for a in data]
+    res = solver.solve(QPData(*tensors))
+    for field in ("y", "status", "iterations", "gradient_eligible"):
+        np.testing.assert_array_equal(getattr(res, field).detach().cpu().numpy(), want[field],
+                                      err_msg=field)
+    q, c, _, _, lower, upper = data
+    free = -c / q
+    ok = np.ones(4, bool)
+    if bad_sample is not None:
+        ok[bad_sample] = False
+    np.testing.assert_allclose(res.y.detach().cpu().numpy()[ok], np.clip(free, lower, upper)[ok],
+                               atol=1e-10)
+    res.y.sum().backward()
+    inside = (free > lower) & (free < upper)
+    expected = np.where(inside, -1.0 / q, 0.0)
+    expected[~ok] = 0.0
+    np.testing.assert_allclose(tensors[1].grad.cpu().numpy(), expected, atol=1e-9)
+
+
+def test_single_sample_batch_matches_oracle():
+    structure, data = random_qp(21, 1, 16, 3, 5, 4, converge=True)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-7)
+    oracle = OracleDiagonalQP(16, structure.equality_rows, structure.inequality_rows,
+                              oracle_config(cfg))
+    want, _ = oracle.solve(data)
+    got = structure.prepare(batch_size=1, config=cfg).solve(
+        QPData(*(torch.as_tensor(a, device=DEV) for a in data)))
+    for field in ("y", "multipliers_eq", "multipliers_ineq", "status", "iterations"):
+        np.testing.assert_array_equal(getattr(got, field).cpu().numpy(), want[field],
+                                      err_msg=field)
