@@ -57,9 +57,9 @@ WORKLOADS = {
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one cp_forward_kernel launch per sample, from the
 # ncu capture of 592 samples in profiles/cp_forward_config2_b592.md
-# ((24.72 MB + 11.5 KB) / 592); the iterates stay on chip, so the traffic is the
-# per-sample inputs and grows with the batch.
-FORWARD_DRAM_BYTES_PER_SAMPLE = (24.716288e6 + 11520.0) / 592
+# ((24.674048 MB + 512 B) / 592); the iterates stay on chip, so the traffic is
+# the per-sample inputs and grows with the batch.
+FORWARD_DRAM_BYTES_PER_SAMPLE = (24.674048e6 + 512.0) / 592
 
 
 def parse_args():
