@@ -361,6 +361,16 @@ int32_t purin_qp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config,
                          const PurinQpAdjointArgs* args, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* purin_qp_adjoint_stage: purin_qp_adjoint one phase per call, with the
+ * phases, counters and driver of purin_cp_adjoint_stage, so that shards of a
+ * QP batch share the reference's batch-wide GMRES budget
+ * (diagonal_qp.py:196-204 -> operators.py:919-1103). */
+int32_t purin_qp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* config,
+                               const PurinLinearSolverConfig* linear,
+                               const PurinQpAdjointArgs* args, int32_t stage,
+                               int32_t completed, int32_t* counters, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* purin_cp_forward_noalloc: the forward solve of purin_cp_forward for callers
  * that cannot allocate device memory -- a plugin or custom-call hook that is
  * given only its input and output buffers, a framework that has reserved

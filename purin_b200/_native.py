@@ -99,6 +99,7 @@ EXPORTED = (
     "purin_cp_plan_destroy", "purin_cp_plan_info", "purin_cp_plan_indices",
     "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_adjoint_stage",
     "purin_cp_postprocess", "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
+    "purin_qp_adjoint_stage",
 )
 
 _lib = None
@@ -144,10 +145,15 @@ def load():
                                      c_vp, ctypes.c_size_t, c_vp]
     lib.purin_qp_adjoint.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(LinearConfig),
                                      ctypes.POINTER(QpAdjointArgs), c_vp, ctypes.c_size_t, c_vp]
+    lib.purin_qp_adjoint_stage.argtypes = [c_vp, ctypes.POINTER(CpConfig),
+                                           ctypes.POINTER(LinearConfig),
+                                           ctypes.POINTER(QpAdjointArgs), c_i32, c_i32, c_vp, c_vp,
+                                           ctypes.c_size_t, c_vp]
     for name in ("purin_cp_plan_create", "purin_cp_plan_destroy", "purin_cp_plan_info",
                  "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward",
                  "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess",
-                 "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint"):
+                 "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
+                 "purin_qp_adjoint_stage"):
         getattr(lib, name).restype = c_i32
     version = lib.purin_cp_abi_version()
     if version != ABI_VERSION:
@@ -227,6 +233,13 @@ class Plan:
         check(self._lib.purin_qp_adjoint(self.handle, ctypes.byref(cfg), ctypes.byref(lin),
                                          ctypes.byref(args), workspace_ptr, workspace_bytes,
                                          stream), "purin_qp_adjoint")
+
+    def qp_adjoint_stage(self, cfg, lin, args, stage, completed, counters_ptr, workspace_ptr,
+                         workspace_bytes, stream):
+        check(self._lib.purin_qp_adjoint_stage(self.handle, ctypes.byref(cfg), ctypes.byref(lin),
+                                               ctypes.byref(args), stage, completed, counters_ptr,
+                                               workspace_ptr, workspace_bytes, stream),
+              "purin_qp_adjoint_stage")
 
     def postprocess(self, args, stream):
         check(self._lib.purin_cp_postprocess(self.handle, ctypes.byref(args), stream),

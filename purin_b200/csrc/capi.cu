@@ -436,6 +436,18 @@ struct QpAdjoint {
 };
 
 template <typename T>
+void set_qp(purin::AdjParams<T>& p, const QpAdjoint* qp, const PurinCpConfig* cfg) {
+  if (!qp) return;
+  p.qp = 1;
+  p.q = static_cast<const T*>(qp->q);
+  p.c = static_cast<const T*>(qp->c);
+  p.cot_dual = static_cast<const T*>(qp->cot_dual);
+  p.g_q = static_cast<T*>(qp->grad_q);
+  p.g_c = static_cast<T*>(qp->grad_c);
+  p.norm_bound = cfg->norm_bound ? 1 : 0;
+}
+
+template <typename T>
 int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                     const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
                     cudaStream_t stream, const QpAdjoint* qp = nullptr) {
@@ -450,15 +462,7 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   e = cudaMemsetAsync(a->device_error, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
   purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
-  if (qp) {
-    p.qp = 1;
-    p.q = static_cast<const T*>(qp->q);
-    p.c = static_cast<const T*>(qp->c);
-    p.cot_dual = static_cast<const T*>(qp->cot_dual);
-    p.g_q = static_cast<T*>(qp->grad_q);
-    p.g_c = static_cast<T*>(qp->grad_c);
-    p.norm_bound = cfg->norm_bound ? 1 : 0;
-  }
+  set_qp(p, qp, cfg);
   e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch");
   return PURIN_OK;
@@ -472,8 +476,9 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
 template <typename T>
 int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                           const PurinCpAdjointArgs* a, int32_t stage, int32_t completed, int32_t* counters,
-                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch);
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                          const QpAdjoint* qp = nullptr) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -489,6 +494,7 @@ int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, con
     if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage memset");
   }
   purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
+  set_qp(p, qp, cfg);
   unsigned* words = reinterpret_cast<unsigned*>(counters);
   p.barrier = nullptr;
   p.completed0 = completed;
@@ -625,6 +631,67 @@ int32_t check_adjoint_args(const PurinCpPlan* plan, const PurinCpAdjointArgs* ar
 }
 
 int32_t create_plan(const PurinCpStructure* s, PurinCpPlan** out, bool presolve_bounds);
+
+// purin_qp_adjoint (stage < 0) and purin_qp_adjoint_stage: the QP arguments on
+// the shared adjoint runners.
+int32_t qp_adjoint_call(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
+                        const PurinQpAdjointArgs* args, int32_t stage, int32_t completed, int32_t* counters,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (plan->info.bound_rows != 0)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "purin_qp_adjoint needs a plan from purin_qp_plan_create");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (stage >= 0 && stage != PURIN_CP_STAGE_FINISH && !counters)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "counters is NULL");
+  if (stage == PURIN_CP_STAGE_CYCLE && (completed < 0 || completed >= linear->max_iterations))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "completed must lie in [0, max_iterations) for a cycle");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (args->batch == 0) {
+    if (stage < 0 || stage == PURIN_CP_STAGE_FINISH) return PURIN_OK;
+    cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(int32_t), s);
+    return e == cudaSuccess ? PURIN_OK : cuda_fail(e, "purin_qp_adjoint_stage memset");
+  }
+  if (!args->q || !args->c) return fail(PURIN_ERR_INVALID_ARGUMENT, "a required QP adjoint array is NULL");
+  PurinCpAdjointArgs a{};
+  a.batch = args->batch;
+  a.values = args->values;
+  a.values_stride = args->values_stride;
+  a.rhs = args->rhs;
+  a.target = args->c;  // satisfies the shared check; the QP kernels read c through QpAdjoint
+  a.lower = args->lower;
+  a.upper = args->upper;
+  a.bounds_stride = args->bounds_stride;
+  a.y = args->y;
+  a.dual = args->dual;
+  a.converged = args->converged;
+  a.cot_y = args->cot_y;
+  a.sample_offset = args->sample_offset;
+  a.total_batch = args->total_batch;
+  a.grad_values = args->grad_values;
+  a.grad_rhs = args->grad_rhs;
+  a.grad_target = nullptr;
+  a.grad_lower = args->grad_lower;
+  a.grad_upper = args->grad_upper;
+  a.linear_status = args->linear_status;
+  a.linear_residual = args->linear_residual;
+  a.device_error = args->device_error;
+  if (int32_t r = check_adjoint_args(plan, &a)) return r;
+  const QpAdjoint qp{args->q, args->c, args->cot_dual, args->grad_q, args->grad_c};
+  const bool f64 = plan->info.dtype == PURIN_FLOAT64;
+  if (stage < 0)
+    return f64 ? run_adjoint<double>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp)
+               : run_adjoint<float>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp);
+  return f64 ? run_adjoint_stage<double>(plan, config, linear, &a, stage, completed, counters, workspace,
+                                         workspace_bytes, s, &qp)
+             : run_adjoint_stage<float>(plan, config, linear, &a, stage, completed, counters, workspace,
+                                        workspace_bytes, s, &qp);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1070,46 +1137,17 @@ int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, c
 
 int32_t purin_qp_adjoint(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinLinearSolverConfig* linear,
                          const PurinQpAdjointArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int32_t r = check_plan(plan)) return r;
-  if (int32_t r = check_config(config)) return r;
-  if (int32_t r = check_linear(linear)) return r;
-  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
-  if (plan->info.bound_rows != 0)
-    return fail(PURIN_ERR_INVALID_ARGUMENT, "purin_qp_adjoint needs a plan from purin_qp_plan_create");
-  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
-  if (args->batch == 0) return PURIN_OK;
-  if (!args->q || !args->c) return fail(PURIN_ERR_INVALID_ARGUMENT, "a required QP adjoint array is NULL");
-  PurinCpAdjointArgs a{};
-  a.batch = args->batch;
-  a.values = args->values;
-  a.values_stride = args->values_stride;
-  a.rhs = args->rhs;
-  a.target = args->c;  // satisfies the shared check; the QP kernels read c through QpAdjoint
-  a.lower = args->lower;
-  a.upper = args->upper;
-  a.bounds_stride = args->bounds_stride;
-  a.y = args->y;
-  a.dual = args->dual;
-  a.converged = args->converged;
-  a.cot_y = args->cot_y;
-  a.sample_offset = args->sample_offset;
-  a.total_batch = args->total_batch;
-  a.grad_values = args->grad_values;
-  a.grad_rhs = args->grad_rhs;
-  a.grad_target = nullptr;
-  a.grad_lower = args->grad_lower;
-  a.grad_upper = args->grad_upper;
-  a.linear_status = args->linear_status;
-  a.linear_residual = args->linear_residual;
-  a.device_error = args->device_error;
-  if (int32_t r = check_adjoint_args(plan, &a)) return r;
-  const QpAdjoint qp{args->q, args->c, args->cot_dual, args->grad_q, args->grad_c};
-  DeviceGuard guard(plan->info.device);
-  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return plan->info.dtype == PURIN_FLOAT64
-             ? run_adjoint<double>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp)
-             : run_adjoint<float>(plan, config, linear, &a, workspace, workspace_bytes, s, &qp);
+  return qp_adjoint_call(plan, config, linear, args, -1, 0, nullptr, workspace, workspace_bytes, stream);
+}
+
+int32_t purin_qp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* config,
+                               const PurinLinearSolverConfig* linear, const PurinQpAdjointArgs* args,
+                               int32_t stage, int32_t completed, int32_t* counters, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (stage != PURIN_CP_STAGE_PREPARE && stage != PURIN_CP_STAGE_CYCLE && stage != PURIN_CP_STAGE_FINISH)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown adjoint stage");
+  return qp_adjoint_call(plan, config, linear, args, stage, completed, counters, workspace, workspace_bytes,
+                         stream);
 }
 
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args, void* stream) {

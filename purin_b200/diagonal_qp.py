@@ -24,7 +24,7 @@ from typing import NamedTuple
 import numpy as np
 import torch
 
-from purin_b200 import _native
+from purin_b200 import _native, lockstep
 from purin_b200.config import ChambollePockConfig
 from purin_b200.layer import _ptr, ctypes_stream, resolve_device, resolve_dtype
 from purin_b200.types import ProjectionResult, SolveStatus
@@ -121,40 +121,89 @@ class _QPSolve(torch.autograd.Function):
     def backward(ctx, gy, gdual, *unused):
         q, c, values, rhs, lower, upper, y, dual, converged = ctx.saved_tensors
         layer = ctx.layer
-        need = ctx.needs_input_grad
-        batch, n = q.shape
         m = rhs.shape[1]
-        dev, dt = q.device, q.dtype
         gy = torch.zeros_like(y) if gy is None else gy.contiguous()
         cot_dual = None
         if layer.differentiate_duals and gdual is not None and m > 0:
             cot_dual = gdual.contiguous()
+        shard = _QPAdjointShard(layer, (q, c, values, rhs, lower, upper, y, dual, converged),
+                                gy, cot_dual, ctx.needs_input_grad)
+        if layer._lockstep_group is None:
+            grads = shard.fused()
+        else:
+            (grads,), _, _ = lockstep.run([shard], int(layer._lin.max_iterations),
+                                          group=layer._lockstep_group)
+        return (*grads, None, None, None, None)
+
+
+class _QPAdjointShard:
+    """Outputs, workspace and C-ABI arguments of one QP adjoint call.
+
+    ``fused()`` is ``purin_qp_adjoint``; ``prepare``/``cycle``/``finish`` are the
+    phases of ``purin_qp_adjoint_stage`` for ``purin_b200.lockstep.run``.
+    """
+
+    def __init__(self, layer, saved, gy, cot_dual, need):
+        q, c, values, rhs, lower, upper, y, dual, converged = saved
+        batch, n = q.shape
+        m = rhs.shape[1]
+        dev, dt = q.device, q.dtype
         out = lambda k, shape: torch.empty(shape, dtype=dt, device=dev) if need[k] else None
-        shared = values.shape[0] == 1 and batch != 1
-        grads = (out(0, (batch, n)), out(1, (batch, n)), out(2, (batch, values.shape[1])),
-                 out(3, (batch, m)), out(4, (batch, n)), out(5, (batch, n)))
-        status = torch.empty((batch,), dtype=torch.int32, device=dev)
-        lres = torch.empty((batch,), dtype=dt, device=dev)
-        err = torch.zeros((1,), dtype=torch.int32, device=dev)
-        ws_bytes = layer._plan.workspace_size(_native.QP_OP_ADJOINT, batch, layer._cfg, layer._lin)
-        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
-        g_q, g_c, g_values, g_rhs, g_lower, g_upper = grads
-        args = _native.QpAdjointArgs(
-            batch, _ptr(q), _ptr(c), _ptr(values), 0 if shared else values.shape[1], _ptr(rhs),
-            _ptr(lower),
-            _ptr(upper), n, _ptr(y), _ptr(dual), _ptr(converged), _ptr(gy), _ptr(cot_dual),
-            layer._sample_offset, layer._total_batch, _ptr(g_q), _ptr(g_c), _ptr(g_values),
-            _ptr(g_rhs), _ptr(g_lower), _ptr(g_upper), _ptr(status), _ptr(lres), _ptr(err))
-        with layer._timed("adjoint"):
-            layer._plan.qp_adjoint(layer._cfg, layer._lin, args, ws.data_ptr(), ws_bytes,
-                                   layer._stream())
-        object.__setattr__(layer, "_last_linear", (status, lres))
-        if int(err.item()) != 0:
+        self.shared = values.shape[0] == 1 and batch != 1
+        self.grads = (out(0, (batch, n)), out(1, (batch, n)), out(2, (batch, values.shape[1])),
+                      out(3, (batch, m)), out(4, (batch, n)), out(5, (batch, n)))
+        self.layer = layer
+        self.status = torch.empty((batch,), dtype=torch.int32, device=dev)
+        self.lres = torch.empty((batch,), dtype=dt, device=dev)
+        self.err = torch.zeros((1,), dtype=torch.int32, device=dev)
+        self.counters = torch.zeros((2,), dtype=torch.int32, device=dev)
+        self.ws_bytes = layer._plan.workspace_size(_native.QP_OP_ADJOINT, batch, layer._cfg,
+                                                   layer._lin)
+        self.ws = torch.empty((max(self.ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        g_q, g_c, g_values, g_rhs, g_lower, g_upper = self.grads
+        self.args = _native.QpAdjointArgs(
+            batch, _ptr(q), _ptr(c), _ptr(values), 0 if self.shared else values.shape[1],
+            _ptr(rhs), _ptr(lower), _ptr(upper), n, _ptr(y), _ptr(dual), _ptr(converged),
+            _ptr(gy), _ptr(cot_dual), layer._sample_offset, layer._total_batch, _ptr(g_q),
+            _ptr(g_c), _ptr(g_values), _ptr(g_rhs), _ptr(g_lower), _ptr(g_upper),
+            _ptr(self.status), _ptr(self.lres), _ptr(self.err))
+        # Keep every buffer the arguments point at alive for the shard's lifetime.
+        self._inputs = (saved, gy, cot_dual)
+
+    def _done(self):
+        object.__setattr__(self.layer, "_last_linear", (self.status, self.lres))
+        if int(self.err.item()) != 0:
             raise RuntimeError("purin_qp_adjoint: a bounded device wait timed out; "
                                "gradients are invalid")
-        if shared and g_values is not None:
+        g_q, g_c, g_values, g_rhs, g_lower, g_upper = self.grads
+        if self.shared and g_values is not None:
             g_values = g_values.sum(dim=0, keepdim=True)
-        return (g_q, g_c, g_values, g_rhs, g_lower, g_upper, None, None, None, None)
+        return g_q, g_c, g_values, g_rhs, g_lower, g_upper
+
+    def fused(self):
+        layer = self.layer
+        with layer._timed("adjoint"):
+            layer._plan.qp_adjoint(layer._cfg, layer._lin, self.args, self.ws.data_ptr(),
+                                   self.ws_bytes, layer._stream())
+        return self._done()
+
+    def _stage(self, stage, completed=0):
+        layer = self.layer
+        with layer._timed("adjoint"):
+            layer._plan.qp_adjoint_stage(layer._cfg, layer._lin, self.args, stage, completed,
+                                         self.counters.data_ptr(), self.ws.data_ptr(),
+                                         self.ws_bytes, layer._stream())
+        return self.counters
+
+    def prepare(self):
+        return self._stage(_native.STAGE_PREPARE)
+
+    def cycle(self, completed):
+        return self._stage(_native.STAGE_CYCLE, completed)
+
+    def finish(self):
+        self._stage(_native.STAGE_FINISH)
+        return self._done()
 
 
 @dataclass(frozen=True, eq=False)
@@ -221,6 +270,7 @@ class PreparedDiagonalQP:
                                           float(cfg.implicit_gradient.adjoint_tolerance)))
         set_("_sample_offset", 0)
         set_("_total_batch", int(self.batch_size))
+        set_("_lockstep_group", None)
         set_("_timers", None)
 
     @property
@@ -231,10 +281,17 @@ class PreparedDiagonalQP:
     def mask(self):
         return self._mask_np
 
-    def set_shard(self, offset: int, total: int):
-        """Rows ``offset..`` of a global batch of ``total`` (the power iteration's PRNG keys)."""
+    def set_shard(self, offset: int, total: int, group=None):
+        """Rows ``offset..`` of a global batch of ``total``.
+
+        The offset selects the power iteration's PRNG keys; ``group`` (a
+        ``torch.distributed`` group of the ranks holding the other shards) makes
+        the backward share the batch-wide GMRES budget, as for the projection
+        layer (``purin_b200.lockstep``).
+        """
         object.__setattr__(self, "_sample_offset", int(offset))
         object.__setattr__(self, "_total_batch", int(total))
+        object.__setattr__(self, "_lockstep_group", group)
 
     def _stream(self):
         return ctypes_stream(torch.cuda.current_stream(self._device))

@@ -220,3 +220,90 @@ def test_single_sample_batch_matches_oracle():
     for field in ("y", "multipliers_eq", "multipliers_ineq", "status", "iterations"):
         np.testing.assert_array_equal(getattr(got, field).cpu().numpy(), want[field],
                                       err_msg=field)
+
+
+def _lockstep_qp_case():
+    structure, data = random_qp(1, 8, 8, 2, 4, 3, converge=True)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-11,
+                              linear_solver=LinearSolverConfig(tolerance=1e-16, atol=0.0))
+    cot = np.random.default_rng(9).normal(size=data[0].shape)
+    return structure, data, cfg, cot
+
+
+def _qp_grads(solver, data, cot, device):
+    tensors = [torch.as_tensor(a, device=device).requires_grad_(True) for a in data]
+    res = solver.solve(QPData(*tensors))
+    (res.y * torch.as_tensor(cot, device=device)).sum().backward()
+    return torch.cat([res.y.detach().reshape(res.y.shape[0], -1)]
+                     + [t.grad.reshape(t.shape[0], -1) for t in tensors], dim=1)
+
+
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_qp_staged_backward_equals_fused_on_one_rank():
+    """set_shard(..., group) runs purin_qp_adjoint_stage through purin_b200.lockstep
+    (one NCCL rank here); the gradients equal the fused purin_qp_adjoint's bit for bit."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    structure, data, cfg, cot = _lockstep_qp_case()
+    want = _qp_grads(structure.prepare(batch_size=8, config=cfg), data, cot, DEV)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    try:
+        solver = structure.prepare(batch_size=8, config=cfg)
+        solver.set_shard(0, 8, group=dist.group.WORLD)
+        got = _qp_grads(solver, data, cot, DEV)
+    finally:
+        dist.destroy_process_group()
+    np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+
+
+def _qp_rank(rank, world, port, out_path):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                            timeout=timedelta(seconds=60))
+    try:
+        structure, data, cfg, cot = _lockstep_qp_case()
+        per = 8 // world
+        lo, hi = rank * per, (rank + 1) * per
+        solver = structure.prepare(batch_size=per, config=cfg, backend=str(device))
+        solver.set_shard(lo, 8, group=dist.group.WORLD)
+        local = _qp_grads(solver, tuple(a[lo:hi] for a in data), cot[lo:hi], device)
+        gathered = [torch.zeros_like(local) for _ in range(world)]
+        dist.all_gather(gathered, local)
+        torch.cuda.synchronize(device)
+        if rank == 0:
+            np.save(out_path, torch.cat(gathered).cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_qp_two_nccl_ranks_reproduce_the_full_batch(tmp_path):
+    import torch.multiprocessing as mp
+
+    out = tmp_path / "qp_gathered.npy"
+    mp.spawn(_qp_rank, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    structure, data, cfg, cot = _lockstep_qp_case()
+    want = _qp_grads(structure.prepare(batch_size=8, config=cfg), data, cot, DEV)
+    np.testing.assert_array_equal(np.load(out), want.cpu().numpy())
