@@ -102,8 +102,8 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t w = dtype_size(plan->info.dtype);
   const bool f64 = plan->info.dtype == PURIN_FLOAT64;
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
-  // Per-variable proximal coefficients: diagonal steps, or a fixed-step QP.
-  const bool pv = diag || (qp && !cfg->accelerated);
+  // Per-variable proximal coefficients in shared memory: diagonal steps only.
+  const bool pv = diag;
   const int n_pos = plan->sell[0].n_pos, m_pos = plan->sell[0].m_pos;
   const size_t per_sample =
       (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) : 0) + (diag ? (m_pos + 1) : 0)) * w;

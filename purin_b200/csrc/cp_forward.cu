@@ -278,8 +278,9 @@ cp_forward_kernel(const FwdParams<T> p) {
   for (int q = 0; q < S; ++q) vals_q[q] = p.values + sample(q) * p.values_stride;
 
   // Per-variable proximal coefficients live in shared memory for diagonal
-  // steps and for a fixed-step diagonal QP (1 / (1 + tau q_j) differs per variable).
-  const bool pv = p.diag || (kQP && !p.accelerated);
+  // steps; a diagonal QP without them recomputes 1 / (1 + tau q_j) from the q_j
+  // it reads anyway (the same operations, so the same values).
+  const bool pv = p.diag;
   // Iterates in internal positions: y, ybar (n_pos + 1), duals (m_pos + 1); the
   // last element of each is the zero that padding entries gather.
   const size_t tile_elems =
@@ -445,18 +446,6 @@ cp_forward_kernel(const FwdParams<T> p) {
       qmin[q] = -nmin[q];
       if (tid == 0) sc.valid[q] = (qmin[q] > zero && bad[q] == zero) ? 1 : 0;
     }
-    if (!p.diag && !p.accelerated) {
-      // Fixed-step proximal coefficients (kernels.py:68-73, precomputed at 236).
-      for (int pp = tid; pp < n_pos; pp += kThreads) {
-#pragma unroll
-        for (int q = 0; q < S; ++q) {
-          const T tau = safety / (qmax[q] + L[q]);
-          const T a = one / (one + tau * p.q_i[sample(q) * n_pos + pp]);
-          av[(size_t)pp * S + q] = a;
-          dv[(size_t)pp * S + q] = tau * a;
-        }
-      }
-    }
   }
 
   // ---- initial state: y = ybar = y0 (the target), lambda = dual0 -----------
@@ -588,8 +577,10 @@ cp_forward_kernel(const FwdParams<T> p) {
           const T c = kQP ? tg[q] : -tg[q];
           const T qj = qv[q];
           T aa, dd;
-          if (kQP && p.accelerated) {
-            // Accelerated steps change tau: proximal_coefficients every iteration.
+          if (kQP && !p.diag) {
+            // proximal_coefficients (kernels.py:68-73) of this iteration's tau:
+            // fixed steps precompute them (kernels.py:236), accelerated steps
+            // recompute them; either way these are the same operations.
             aa = one / (one + tau_s[q] * qj);
             dd = tau_s[q] * aa;
           } else {
