@@ -407,6 +407,18 @@ purin::AdjParams<T> adjoint_params(const PurinCpPlan* plan, const PurinCpConfig*
   p.R = L.R;
   p.max_it = lin->max_iterations;
   p.timeout_ns = kBarrierTimeoutNs;
+  p.barrier_extra = 0;
+  // Failure-detection test: PURIN_CP_TEST_UNREACHABLE_BARRIER=<ms> makes the
+  // fused kernel's grid barrier wait for one arrival more than the grid has, so
+  // the bounded wait gives up after <ms> milliseconds and the call reports it
+  // through device_error (the context stays usable).
+  if (const char* env = std::getenv("PURIN_CP_TEST_UNREACHABLE_BARRIER")) {
+    const long ms = std::atol(env);
+    if (ms > 0) {
+      p.barrier_extra = 1;
+      p.timeout_ns = (uint64_t)ms * 1000000ull;
+    }
+  }
   p.x = reinterpret_cast<T*>(ws + L.off_x);
   p.lamp = reinterpret_cast<T*>(ws + L.off_lamp);
   p.steps = reinterpret_cast<T*>(ws + L.off_steps);

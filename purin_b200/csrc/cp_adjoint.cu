@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
   T* V = p.basis + (size_t)blockIdx.x * (R + 1) * W;
   const T zero = T(0), one = T(1);
   const T eps = T(1e-30), breakdown = T(1e-14);
-  const unsigned nblocks = gridDim.x;
+  const unsigned nblocks = gridDim.x + p.barrier_extra;
   const int stage = p.stage;
 
   // ---- phase 0: step sizes, linearisation, right-hand side ----------------

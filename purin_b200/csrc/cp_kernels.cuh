@@ -107,6 +107,9 @@ struct AdjParams {
   int R;       // effective restart = min(restart, max_iterations, W)
   int max_it;  // GMRES iteration budget
   uint64_t timeout_ns;
+  // Arrivals the grid barrier waits for beyond gridDim.x: 0, or 1 in the test
+  // that makes a bounded wait run out (PURIN_CP_TEST_UNREACHABLE_BARRIER).
+  unsigned barrier_extra;
   // 0: the whole VJP in one cooperative launch (grid barriers between phases).
   // 1, 2, 3: one phase per launch (prepare; one GMRES cycle; pullback) for a
   // host that exchanges the cycle counters with other shards between launches.

@@ -302,17 +302,19 @@ class PreparedDiagonalQP:
 
     @contextlib.contextmanager
     def _timed(self, name):
+        """NVTX range around one native call; with ``record_launches`` also CUDA events."""
         timers = self._timers
-        if timers is None:
+        with torch.cuda.nvtx.range("purin_qp_" + name):
+            if timers is None:
+                yield
+                return
+            stream = torch.cuda.current_stream(self._device)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
             yield
-            return
-        stream = torch.cuda.current_stream(self._device)
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        yield
-        end.record(stream)
-        timers.append((name, start, end))
+            end.record(stream)
+            timers.append((name, start, end))
 
     # -- ordered sparse products (the reference's accumulation order) -------------
     def _matvec(self, values, x):

@@ -246,17 +246,19 @@ class PreparedChambollePockProjection:
 
     @contextlib.contextmanager
     def _timed(self, name):
+        """NVTX range around one native call; with ``record_launches`` also CUDA events."""
         timers = self._timers
-        if timers is None:
+        with torch.cuda.nvtx.range("purin_cp_" + name):
+            if timers is None:
+                yield
+                return
+            stream = torch.cuda.current_stream(self._device)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
             yield
-            return
-        stream = torch.cuda.current_stream(self._device)
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        yield
-        end.record(stream)
-        timers.append((name, start, end))
+            end.record(stream)
+            timers.append((name, start, end))
 
     def _forward_native(self, data, rhs, target, lower, upper, initial, tolerance, feasible,
                         y, dual, iterations, residual, gap, converged):

@@ -289,3 +289,47 @@ def test_parameter_dependent_coefficients_per_sample():
                   "status", "iterations"):
         np.testing.assert_array_equal(getattr(got, field).cpu().numpy(), expected[field],
                                       err_msg=field)
+
+
+def test_bounded_device_wait_reports_and_context_stays_usable(monkeypatch):
+    """A grid barrier that can never complete (one arrival more than the grid has,
+    PURIN_CP_TEST_UNREACHABLE_BARRIER) gives up after its time limit: the call
+    raises on the host through device_error, and the next call on the same
+    context gives the oracle's gradients."""
+    problem, theta, target = _converging_problem(1)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-11)
+    oracle = OracleLayer(problem, cfg)
+    expected, saved = oracle.solve(target, theta)
+    cot = np.random.default_rng(101).normal(size=target.shape)
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    layer = _layer(problem, cfg, target.shape[0], torch.float64)
+    monkeypatch.setenv("PURIN_CP_TEST_UNREACHABLE_BARRIER", "50")
+    with pytest.raises(RuntimeError, match="bounded device wait"):
+        boundary_adjoint(layer, oracle, saved, cot)
+    monkeypatch.delenv("PURIN_CP_TEST_UNREACHABLE_BARRIER")
+    got, status, _ = boundary_adjoint(layer, oracle, saved, cot)
+    np.testing.assert_array_equal(status, stats["code"])
+    for key in ("rhs", "target", "lower", "upper"):
+        np.testing.assert_allclose(got[key], want[key], rtol=0, atol=1e-9, err_msg=key)
+
+
+def test_gmres_budget_of_one_matches_oracle():
+    """LinearSolverConfig(max_iterations=1): one Arnoldi step per solve; status codes,
+    residual-gated gradients (bounds.py:148-154) and budget as in the oracle."""
+    problem, theta, target = _converging_problem(3)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-11,
+                              linear_solver=LinearSolverConfig(max_iterations=1))
+    oracle = OracleLayer(problem, cfg)
+    expected, saved = oracle.solve(target, theta)
+    assert expected["gradient_eligible"].any()
+    cot = np.random.default_rng(103).normal(size=target.shape)
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    assert stats["completed"] == 1
+    layer = _layer(problem, cfg, target.shape[0], torch.float64)
+    got, status, lres = boundary_adjoint(layer, oracle, saved, cot)
+    np.testing.assert_array_equal(status, stats["code"])
+    np.testing.assert_allclose(lres, stats["residual"], rtol=1e-9, atol=1e-14)
+    for key in ("rhs", "target", "lower", "upper"):
+        np.testing.assert_allclose(got[key], want[key], rtol=0, atol=1e-9, err_msg=key)

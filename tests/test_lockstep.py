@@ -173,3 +173,40 @@ def test_two_gloo_ranks_reproduce_the_full_batch(case, tmp_path):
     np.testing.assert_array_equal(gathered[:, width], stats["code"])
     np.testing.assert_array_equal(gathered[:, width + 1:],
                                   np.tile([stats["completed"], stats["cycles"]], (BATCH, 1)))
+
+
+def _dropping_worker(rank, world, port, out_path):
+    """Rank 1 leaves between steps without joining the exchange; rank 0's lockstep
+    all-reduce must end with an error (connection closed or the group's short
+    timeout), not wait forever."""
+    import json
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)
+    problem, cfg, theta, target, cot = lockstep_case()
+    layer = OracleLayer(problem, cfg)
+    _, shard = _shard(layer, theta, target, cot, 0, HALF)
+    t0 = time.time()
+    try:
+        lockstep.run([shard], 100, group=dist.group.WORLD)
+        outcome = "completed"
+    except Exception as exc:  # the failure the peer's departure must surface
+        outcome = f"error {type(exc).__name__}"
+    with open(out_path, "w") as f:
+        json.dump({"outcome": outcome, "seconds": time.time() - t0}, f)
+    os._exit(0)
+
+
+def test_dropped_rank_ends_the_exchange_with_an_error(tmp_path):
+    import json
+
+    out = tmp_path / "dropped.json"
+    mp.spawn(_dropping_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    result = json.loads(out.read_text())
+    assert result["outcome"].startswith("error"), result
+    assert result["seconds"] < 60
