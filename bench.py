@@ -84,6 +84,9 @@ def parse_args():
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
                         "a loose value such as 1e-3 lets samples converge so that the VJP "
                         "runs full GMRES solves instead of being gated to zero")
+    p.add_argument("--qp-values", default="shared", choices=["shared", "per-sample"],
+                   help="qp: one constraint matrix for the batch (a broadcast view) or a "
+                        "separate copy per sample (the same values, materialised)")
     p.add_argument("--problem", default="projection", choices=["projection", "qp"],
                    help="qp: configuration 2's structure as a general diagonal QP "
                         "(PreparedDiagonalQP), fwd + VJP w.r.t. q, c, values, rhs and bounds")
@@ -289,12 +292,16 @@ def main_qp(args, world, rank, local_rank, device, barrier):
     dev = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device=device)
     q_d, c_d, rhs_d, t_d = dev(q), dev(c), dev(rhs), dev(targets)
     vals_d, lo_d, up_d = dev(values), dev(lower)[None], dev(upper)[None]
+    if args.qp_values == "per-sample":
+        vals_d = vals_d.expand(batch, -1, -1).contiguous()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
     def step(q_, c_, rhs_, t_):
         # The constraint matrix and the bounds are shared by the batch (stride-0 views).
         leaves = [x.detach().requires_grad_(True) for x in (q_, c_, vals_d, rhs_, lo_d, up_d)]
-        data = QPData(leaves[0], leaves[1], leaves[2].expand(batch, -1, -1), leaves[3],
+        values = (leaves[2].expand(batch, -1, -1) if vals_d.shape[0] == 1
+                  else leaves[2])
+        data = QPData(leaves[0], leaves[1], values, leaves[3],
                       leaves[4].expand(batch, -1), leaves[5].expand(batch, -1))
         res = solver.solve(data)
         loss = 0.5 * ((res.y - t_) ** 2).sum()
@@ -337,7 +344,8 @@ def main_qp(args, world, rank, local_rank, device, barrier):
     fwd_ms, adj_ms = per_step("forward"), per_step("adjoint")
     launches = count_native_launches(lambda: step(q_d, c_d, rhs_d, t_d), device) * args.steps
     with torch.no_grad():
-        res = solver.solve(QPData(q_d, c_d, vals_d.expand(batch, -1, -1), rhs_d,
+        res = solver.solve(QPData(q_d, c_d, vals_d.expand(batch, -1, -1) if vals_d.shape[0] == 1
+                                  else vals_d, rhs_d,
                                   lo_d.expand(batch, -1), up_d.expand(batch, -1)))
     iters_total = int(res.iterations.sum().item())
     eligible = int(res.gradient_eligible.sum().item())
@@ -390,7 +398,8 @@ def main_qp(args, world, rank, local_rank, device, barrier):
             "data": "synthetic (configuration 2's seeded structure as a diagonal QP; no dataset)",
             "config": {
                 "workload": "qp: PreparedDiagonalQP, fp64, n=2048, me=512, mi=1024, 8 nnz/row "
-                            "(values shared by the batch), per-sample q~U(0.5,2), c=-q*candidate, "
+                            f"(values {'shared by the batch' if args.qp_values == 'shared' else 'per sample'}"
+                            "), per-sample q~U(0.5,2), c=-q*candidate, "
                             "rhs; bounds shared; 2000 fixed-step CP iterations (tolerance "
                             f"{cfg.tolerance:g} stopping test kept); loss 0.5||y-t||^2, "
                             "gradients w.r.t. q, c, values, rhs, lower, upper",

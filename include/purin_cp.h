@@ -68,7 +68,12 @@ typedef enum PurinCpOp {
   PURIN_CP_OP_FORWARD = 0,
   PURIN_CP_OP_ADJOINT = 1,
   PURIN_QP_OP_FORWARD = 2, /* purin_qp_forward */
-  PURIN_QP_OP_ADJOINT = 3  /* purin_qp_adjoint */
+  PURIN_QP_OP_ADJOINT = 3, /* purin_qp_adjoint */
+  /* The forward solves with values given per sample (values_stride != 0): the
+   * workspace also holds each sample's values in the kernels' two sparse orders.
+   * The FORWARD ops size the workspace for values shared by the batch. */
+  PURIN_CP_OP_FORWARD_SAMPLE_VALUES = 4,
+  PURIN_QP_OP_FORWARD_SAMPLE_VALUES = 5
 } PurinCpOp;
 
 /* Index arrays derived by the plan (purin_cp_plan_indices). */

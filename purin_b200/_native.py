@@ -17,6 +17,7 @@ ABI_VERSION = 1
 
 PURIN_FLOAT64, PURIN_FLOAT32 = 0, 1
 OP_FORWARD, OP_ADJOINT, QP_OP_FORWARD, QP_OP_ADJOINT = 0, 1, 2, 3
+OP_FORWARD_SAMPLE_VALUES, QP_OP_FORWARD_SAMPLE_VALUES = 4, 5
 STAGE_PREPARE, STAGE_CYCLE, STAGE_FINISH = 0, 1, 2
 KEPT_ROWS, KEPT_SLOTS, BOUND_ROWS, BOUND_SLOTS, BOUND_VARIABLES, KEPT_ROW_PTR, KEPT_COLS = range(7)
 

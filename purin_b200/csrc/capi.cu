@@ -62,14 +62,16 @@ struct FwdPlan {
   size_t off_vr = 0, off_vc = 0, off_state = 0;
   size_t off_tgt = 0, off_rhs = 0, off_dual0 = 0, off_lo = 0, off_up = 0;
   size_t off_q = 0, off_c = 0, off_y0 = 0;  // diagonal QP inputs (internal order)
+  size_t off_vr_ps = 0, off_vc_ps = 0;      // per-sample values in the SELL orders
   int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
 
 FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
                            bool shared_values, bool qp);
 
-// The workspace does not depend on shared_values: it only ranks tile widths
-// whose state fits in shared memory, which need no workspace for the state.
+// Values shared by the batch are arranged into the two SELL orders once; values
+// given per sample are arranged per sample, which the workspace must then hold
+// (PURIN_CP_OP_FORWARD_SAMPLE_VALUES / PURIN_QP_OP_FORWARD_SAMPLE_VALUES).
 FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t batch,
                      bool shared_values = true, bool qp = false) {
   FwdPlan fp = plan_forward_tiles(const_cast<PurinCpPlan*>(plan), cfg, batch, shared_values, qp);
@@ -91,7 +93,10 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   fp.off_q = fp.off_up + align_up(nb * sv.n_pos * w);
   fp.off_c = fp.off_q + qp_vec;
   fp.off_y0 = fp.off_c + qp_vec;
-  fp.off_state = fp.off_y0 + qp_vec;
+  const size_t ps = shared_values ? 0 : nb;
+  fp.off_vr_ps = fp.off_y0 + qp_vec;
+  fp.off_vc_ps = fp.off_vr_ps + align_up(ps * sv.nnz_r * w);
+  fp.off_state = fp.off_vc_ps + align_up(ps * sv.nnz_c * w);
   fp.workspace = fp.off_state + fp.workspace;
   return fp;
 }
@@ -262,10 +267,12 @@ template <typename T>
 int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinCpForwardArgs* a,
                     void* workspace, size_t workspace_bytes, cudaStream_t stream,
                     const QpInputs* qp = nullptr) {
-  const bool shared = a->values_stride == 0 || a->batch == 1;
+  const bool shared = a->values_stride == 0 || a->batch == 1 || plan->info.kept_nnz == 0;
   const FwdPlan fp = plan_forward(plan, cfg, a->batch, shared, qp != nullptr);
   if (workspace == nullptr || workspace_bytes < fp.workspace)
-    return fail(PURIN_ERR_WORKSPACE, "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes");
+    return fail(PURIN_ERR_WORKSPACE,
+                "forward workspace too small: need " + std::to_string(fp.workspace) + " bytes" +
+                    (shared ? "" : " for values given per sample (size it with the *_SAMPLE_VALUES op)"));
   char* ws = static_cast<char*>(workspace);
   const purin::SellView& sv = plan->sell[fp.sell_index];
   // Values shared by the batch are arranged once per call in both sliced-ELL orders.
@@ -278,6 +285,21 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
     if (e == cudaSuccess)
       e = purin::arrange_values<T>(static_cast<const T*>(a->values), sv.c_slot, sv.nnz_c, vc, stream);
     if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward value layout");
+  }
+  // Values given per sample: each sample's copy in both SELL orders, so the solve
+  // reads them coalesced and without the slot indirection.
+  T* vr_ps = nullptr;
+  T* vc_ps = nullptr;
+  if (!shared) {
+    vr_ps = reinterpret_cast<T*>(ws + fp.off_vr_ps);
+    vc_ps = reinterpret_cast<T*>(ws + fp.off_vc_ps);
+    const T* vals = static_cast<const T*>(a->values);
+    cudaError_t e = purin::arrange_sample_values<T>(vals, a->values_stride, sv.r_slot, sv.nnz_r, a->batch,
+                                                    vr_ps, stream);
+    if (e == cudaSuccess)
+      e = purin::arrange_sample_values<T>(vals, a->values_stride, sv.c_slot, sv.nnz_c, a->batch, vc_ps,
+                                          stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward per-sample value layout");
   }
   // Per-sample inputs in the internal row/column orders (coalesced per-iteration reads).
   T* tgt_i = reinterpret_cast<T*>(ws + fp.off_tgt);
@@ -362,6 +384,10 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.sell = sv;
   p.vr = vr;
   p.vc = vc;
+  p.vr_ps = vr_ps;
+  p.vc_ps = vc_ps;
+  p.nnz_r_ps = sv.nnz_r;
+  p.nnz_c_ps = sv.nnz_c;
   cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.NT, fp.smem, fp.smem_bytes, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward launch");
   return PURIN_OK;
@@ -1017,6 +1043,10 @@ int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t bat
     *bytes = plan_forward(plan, config, batch, true, true).workspace;
     return PURIN_OK;
   }
+  if (op == PURIN_CP_OP_FORWARD_SAMPLE_VALUES || op == PURIN_QP_OP_FORWARD_SAMPLE_VALUES) {
+    *bytes = plan_forward(plan, config, batch, batch == 1, op == PURIN_QP_OP_FORWARD_SAMPLE_VALUES).workspace;
+    return PURIN_OK;
+  }
   if (op == PURIN_CP_OP_ADJOINT || op == PURIN_QP_OP_ADJOINT) {
     if (int32_t r = check_linear(linear)) return r;
     const AdjLayout L = plan_adjoint(plan, config, linear, batch, op == PURIN_QP_OP_ADJOINT);
@@ -1220,7 +1250,8 @@ extern "C" int32_t purin_cp_forward_noalloc(const PurinCpPlan* plan, const Purin
   const int device = plan->info.device;
   if (device < 0 || device >= kNoAllocMaxDevices)
     return fail(PURIN_ERR_UNSUPPORTED, "purin_cp_forward_noalloc supports device ordinals below 128");
-  const size_t need = plan_forward(plan, config, args->batch).workspace;
+  const bool shared = args->values_stride == 0 || args->batch == 1 || plan->info.kept_nnz == 0;
+  const size_t need = plan_forward(plan, config, args->batch, shared).workspace;
   if (need > kNoAllocScratchBytes)
     return fail(PURIN_ERR_WORKSPACE,
                 "purin_cp_forward_noalloc needs " + std::to_string(need) +

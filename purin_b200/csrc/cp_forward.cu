@@ -99,7 +99,7 @@ struct SellLines {
   const uint32_t* idx2;
   const int* slot;
   const T* sell_vals;    // kShared: values in SELL order
-  const T* const* vals;  // !kShared: per-sample value rows (CSR slot order)
+  const T* const* vals;  // !kShared: each sample's values in this SELL order
 
   __device__ __forceinline__ void step(int e, int col, const T* x, T (&acc)[S]) const {
     T xs[S];
@@ -109,12 +109,8 @@ struct SellLines {
 #pragma unroll
       for (int q = 0; q < S; ++q) acc[q] = acc[q] + v * xs[q];
     } else {
-      const int s0 = __ldg(slot + e);
 #pragma unroll
-      for (int q = 0; q < S; ++q) {
-        const T v = s0 >= 0 ? vals[q][s0] : T(0);
-        acc[q] = acc[q] + v * xs[q];
-      }
+      for (int q = 0; q < S; ++q) acc[q] = acc[q] + vals[q][e] * xs[q];
     }
   }
 
@@ -151,9 +147,8 @@ struct SellLines {
 #pragma unroll
         for (int q = 0; q < S; ++q) acc[q] = acc[q] + v;
       } else {
-        const int s0 = __ldg(slot + e);
 #pragma unroll
-        for (int q = 0; q < S; ++q) acc[q] = acc[q] + fabs(s0 >= 0 ? vals[q][s0] : T(0)) * T(1);
+        for (int q = 0; q < S; ++q) acc[q] = acc[q] + fabs(vals[q][e]) * T(1);
       }
     }
   }
@@ -273,9 +268,15 @@ cp_forward_kernel(const FwdParams<T> p) {
   const int64_t tile0 = (int64_t)blockIdx.x * S;
   auto sample = [&](int q) -> int64_t { return tile0 + q < p.batch ? tile0 + q : p.batch - 1; };
   auto is_valid = [&](int q) -> bool { return tile0 + q < p.batch; };
-  const T* vals_q[S];
+  // Per-sample values (not shared): each sample's copy in the two SELL orders
+  // (arranged once per call; padding entries hold zeros).
+  const T* vr_q[S];
+  const T* vc_q[S];
 #pragma unroll
-  for (int q = 0; q < S; ++q) vals_q[q] = p.values + sample(q) * p.values_stride;
+  for (int q = 0; q < S; ++q) {
+    vr_q[q] = kShared ? nullptr : p.vr_ps + sample(q) * p.nnz_r_ps;
+    vc_q[q] = kShared ? nullptr : p.vc_ps + sample(q) * p.nnz_c_ps;
+  }
 
   // Per-variable proximal coefficients live in shared memory for diagonal
   // steps; a diagonal QP without them recomputes 1 / (1 + tau q_j) from the q_j
@@ -295,9 +296,9 @@ cp_forward_kernel(const FwdParams<T> p) {
 
   // Shared-memory tiles read index pairs (positions fit in 16 bits there).
   const SellLines<T, S, kShared, kSmem> rows{sv.r_ptr, sv.r_perm, sv.r_idx, sv.r_idx2, sv.r_slot,
-                                              p.vr, vals_q};
+                                              p.vr, vr_q};
   const SellLines<T, S, kShared, kSmem> cols{sv.c_ptr, sv.c_perm, sv.c_idx, sv.c_idx2, sv.c_slot,
-                                              p.vc, vals_q};
+                                              p.vc, vc_q};
   const T zero = T(0), one = T(1);
   const T safety = p.safety;
 
@@ -850,6 +851,20 @@ __global__ void permute_rows_kernel(const T* src, int64_t src_stride, const int*
   }
 }
 
+// Per-sample values in SELL order: out[b * count + e] = values[b * stride + slot[e]].
+template <typename T>
+__global__ void arrange_sample_values_kernel(const T* values, int64_t stride, const int* slot,
+                                             int count, int64_t batch, T* out) {
+  const int64_t total = batch * (int64_t)count;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / count;
+    const int e = (int)(i - b * count);
+    const int sl = slot[e];
+    out[i] = sl >= 0 ? values[b * stride + sl] : T(0);
+  }
+}
+
 // Shared values in SELL order: out[e] = values[slot[e]] (0 for padding).
 template <typename T>
 __global__ void arrange_values_kernel(const T* values, const int* slot, int count, T* out) {
@@ -970,6 +985,18 @@ cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, 
 }
 
 template <typename T>
+cudaError_t arrange_sample_values(const T* values, int64_t stride, const int* slot, int count,
+                                  int64_t batch, T* out, cudaStream_t stream) {
+  const int64_t total = batch * (int64_t)count;
+  if (total <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const int blocks = want < 4736 ? (int)want : 4736;
+  arrange_sample_values_kernel<T><<<blocks, threads, 0, stream>>>(values, stride, slot, count, batch, out);
+  return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int npos, int64_t rows,
                          T* dst, cudaStream_t stream) {
   const int64_t total = rows * (int64_t)npos;
@@ -1001,6 +1028,10 @@ template size_t forward_static_smem<double>(int, int);
 template size_t forward_static_smem<float>(int, int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);
 template cudaError_t arrange_values<float>(const float*, const int*, int, float*, cudaStream_t);
+template cudaError_t arrange_sample_values<double>(const double*, int64_t, const int*, int, int64_t,
+                                                   double*, cudaStream_t);
+template cudaError_t arrange_sample_values<float>(const float*, int64_t, const int*, int, int64_t,
+                                                  float*, cudaStream_t);
 template cudaError_t permute_rows<double>(const double*, int64_t, const int*, int, int64_t, double*,
                                           cudaStream_t);
 template cudaError_t permute_rows<float>(const float*, int64_t, const int*, int, int64_t, float*,

@@ -42,8 +42,14 @@ struct FwdParams {
   int partitionable;
   T* gstate;  // per-tile state in global memory when it does not fit in shared memory
   SellView sell;  // sliced-ELL rows/columns in the internal orders
-  const T* vr;    // shared values in SELL row order (null: per-sample values via slots)
+  const T* vr;    // shared values in SELL row order (null: per-sample values)
   const T* vc;    // shared values in SELL column order
+  // Per-sample values arranged into the SELL row / column orders once per call,
+  // (B, nnz_r_ps) and (B, nnz_c_ps); used when the values are not shared.
+  const T* vr_ps;
+  const T* vc_ps;
+  int64_t nnz_r_ps;
+  int64_t nnz_c_ps;
   // Per-sample inputs permuted into the internal orders (zero at padding positions).
   const T* tgt_i;    // (B, n_pos)
   const T* rhs_i;    // (B, m_pos)
@@ -177,6 +183,11 @@ template <typename T>
 int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, bool qp = false);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
+// Per-sample values into SELL order: out[b * count + e] = values[b * stride + slot[e]]
+// (0 for padding) for b < batch.
+template <typename T>
+cudaError_t arrange_sample_values(const T* values, int64_t stride, const int* slot, int count,
+                                  int64_t batch, T* out, cudaStream_t stream);
 // dst[b * npos + p] = perm[p] >= 0 ? src[b * src_stride + perm[p]] : 0 for b < rows.
 template <typename T>
 cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int npos, int64_t rows,

@@ -100,11 +100,12 @@ class _QPSolve(torch.autograd.Function):
         residual = torch.empty((batch,), dtype=dt, device=dev)
         gap = torch.empty((batch,), dtype=dt, device=dev)
         converged = torch.empty((batch,), dtype=torch.uint8, device=dev)
-        ws_bytes = layer._plan.workspace_size(_native.QP_OP_FORWARD, batch, layer._cfg)
-        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
         # One row of values for the whole batch (a broadcast constraint matrix) is
         # passed with stride 0; otherwise one row per sample.
         stride = 0 if values.shape[0] == 1 and batch != 1 else values.shape[1]
+        op = _native.QP_OP_FORWARD if stride == 0 else _native.QP_OP_FORWARD_SAMPLE_VALUES
+        ws_bytes = layer._plan.workspace_size(op, batch, layer._cfg)
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
         args = _native.QpForwardArgs(
             batch, _ptr(q), _ptr(c), _ptr(values), stride, _ptr(rhs), _ptr(lower),
             _ptr(upper), n, _ptr(y0), _ptr(dual0), _ptr(tolerance), layer._sample_offset,

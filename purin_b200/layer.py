@@ -263,7 +263,9 @@ class PreparedChambollePockProjection:
     def _forward_native(self, data, rhs, target, lower, upper, initial, tolerance, feasible,
                         y, dual, iterations, residual, gap, converged):
         batch = target.shape[0]
-        ws_bytes = self._plan.workspace_size(_native.OP_FORWARD, batch, self._cfg)
+        per_sample = data.shape[0] != 1 and batch != 1
+        ws_bytes = self._plan.workspace_size(
+            _native.OP_FORWARD_SAMPLE_VALUES if per_sample else _native.OP_FORWARD, batch, self._cfg)
         ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=self._device)
         args = _native.ForwardArgs(
             batch, _ptr(data), 0 if data.shape[0] == 1 and batch != 1 else data.shape[1],
