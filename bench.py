@@ -84,6 +84,8 @@ def parse_args():
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
                         "a loose value such as 1e-3 lets samples converge so that the VJP "
                         "runs full GMRES solves instead of being gated to zero")
+    p.add_argument("--diagonal-preconditioning", action="store_true",
+                   help="ChambollePockConfig(diagonal_preconditioning=True) for fixed-step runs")
     p.add_argument("--qp-values", default="shared", choices=["shared", "per-sample"],
                    help="qp: one constraint matrix for the batch (a broadcast view) or a "
                         "separate copy per sample (the same values, materialised)")
@@ -469,6 +471,8 @@ def main():
         cfg = dataclasses.replace(cfg, metric_diagonal=tuple(float(v) for v in workload.weights))
     if args.cp_tolerance is not None:
         cfg = dataclasses.replace(cfg, tolerance=args.cp_tolerance)
+    if args.diagonal_preconditioning:
+        cfg = dataclasses.replace(cfg, diagonal_preconditioning=True)
     layer = prepare_projection(workload.problem, method="chambolle-pock", config=cfg,
                                batch_size=batch, dtype=tdt, backend=str(device))
     # Ranks > 1 share the adjoint GMRES budget of the whole batch, as the

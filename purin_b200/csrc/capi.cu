@@ -63,6 +63,7 @@ struct FwdPlan {
   size_t off_tgt = 0, off_rhs = 0, off_dual0 = 0, off_lo = 0, off_up = 0;
   size_t off_q = 0, off_c = 0, off_y0 = 0;  // diagonal QP inputs (internal order)
   size_t off_vr_ps = 0, off_vc_ps = 0;      // per-sample values in the SELL orders
+  size_t off_dg = 0;                        // shared diagonal steps (sigma, tau, a, d)
   int sell_index = 0;  // log2(32 / C), C = 32 / S
 };
 
@@ -96,7 +97,10 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t ps = shared_values ? 0 : nb;
   fp.off_vr_ps = fp.off_y0 + qp_vec;
   fp.off_vc_ps = fp.off_vr_ps + align_up(ps * sv.nnz_r * w);
-  fp.off_state = fp.off_vc_ps + align_up(ps * sv.nnz_c * w);
+  // Diagonal steps of shared values: once per call, m_pos + 3 n_pos scalars.
+  const bool dg = cfg->diagonal_preconditioning && !cfg->accelerated && shared_values;
+  fp.off_dg = fp.off_vc_ps + align_up(ps * sv.nnz_c * w);
+  fp.off_state = fp.off_dg + (dg ? align_up((size_t)(sv.m_pos + 3 * (size_t)sv.n_pos) * w) : 0);
   fp.workspace = fp.off_state + fp.workspace;
   return fp;
 }
@@ -107,11 +111,12 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t w = dtype_size(plan->info.dtype);
   const bool f64 = plan->info.dtype == PURIN_FLOAT64;
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
-  // Per-variable proximal coefficients in shared memory: diagonal steps only.
-  const bool pv = diag;
+  // Per-tile diagonal steps in shared memory: only for values given per sample
+  // (with shared values the steps are computed once per call in the workspace).
+  const bool pv = diag && !shared_values;
   const int n_pos = plan->sell[0].n_pos, m_pos = plan->sell[0].m_pos;
   const size_t per_sample =
-      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) : 0) + (diag ? (m_pos + 1) : 0)) * w;
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * w;
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
@@ -142,7 +147,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
       if (NT == want_nt && S <= want_s && (best < 0 || S > kShapes[best][0])) best = k;
       continue;
     }
-    int& cached = plan->fwd_blocks[qp ? (pv ? 3 : 2) : (diag ? 1 : 0)][shared_values ? 1 : 0][k];
+    int& cached = plan->fwd_blocks[qp ? (pv ? 3 : 2) : (pv ? 1 : 0)][shared_values ? 1 : 0][k];
     if (cached < 0) {
       const size_t dyn = (size_t)S * per_sample;
       cached = f64 ? purin::forward_blocks_per_sm<double>(S, NT, shared_values, dyn, qp)
@@ -386,6 +391,17 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.vc = vc;
   p.vr_ps = vr_ps;
   p.vc_ps = vc_ps;
+  if (p.diag && shared) {
+    T* dgp = reinterpret_cast<T*>(ws + fp.off_dg);
+    const int n_pos = sv.n_pos, m_pos = sv.m_pos;
+    p.dg_sigma = dgp;
+    p.dg_tau = dgp + m_pos;
+    p.dg_a = dgp + m_pos + n_pos;
+    p.dg_d = dgp + m_pos + 2 * (size_t)n_pos;
+    cudaError_t e = purin::diagonal_steps<T>(sv, vr, vc, p.safety, dgp, dgp + m_pos, dgp + m_pos + n_pos,
+                                             dgp + m_pos + 2 * (size_t)n_pos, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward diagonal steps");
+  }
   p.nnz_r_ps = sv.nnz_r;
   p.nnz_c_ps = sv.nnz_c;
   cudaError_t e = purin::launch_forward<T>(p, fp.S, fp.NT, fp.smem, fp.smem_bytes, stream);

@@ -281,16 +281,19 @@ cp_forward_kernel(const FwdParams<T> p) {
   // Per-variable proximal coefficients live in shared memory for diagonal
   // steps; a diagonal QP without them recomputes 1 / (1 + tau q_j) from the q_j
   // it reads anyway (the same operations, so the same values).
-  const bool pv = p.diag;
+  // Diagonal steps: shared by the batch in global memory (dg), else per tile in
+  // shared memory (pv).
+  const bool dg = p.dg_sigma != nullptr;
+  const bool pv = p.diag && !dg;
   // Iterates in internal positions: y, ybar (n_pos + 1), duals (m_pos + 1); the
   // last element of each is the zero that padding entries gather.
   const size_t tile_elems =
-      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) : 0) + (p.diag ? (m_pos + 1) : 0)) * S;
+      (size_t)(2 * (n_pos + 1) + (m_pos + 1) + (pv ? 2 * (n_pos + 1) + (m_pos + 1) : 0)) * S;
   T* base = kSmem ? reinterpret_cast<T*>(dyn_smem) : p.gstate + (size_t)blockIdx.x * tile_elems;
   T* y = base;
   T* ybar = y + (size_t)(n_pos + 1) * S;
   T* lam = ybar + (size_t)(n_pos + 1) * S;
-  T* av = lam + (size_t)(m_pos + 1) * S;  // per-variable a, d (only when pv); sigma (p.diag)
+  T* av = lam + (size_t)(m_pos + 1) * S;  // per-variable a, d and per-row sigma (only when pv)
   T* dv = av + (size_t)(n_pos + 1) * S;
   T* sv_ = dv + (size_t)(n_pos + 1) * S;
 
@@ -306,7 +309,7 @@ cp_forward_kernel(const FwdParams<T> p) {
   T L[S];
 #pragma unroll
   for (int q = 0; q < S; ++q) L[q] = one;
-  if (p.diag) {
+  if (pv) {
     // diagonal_step_sizes (kernels.py:76-88): |K| row and column sums.
     for (int sl = warp; sl < sv.nsl_r; sl += kWarps) {
       T acc[S];
@@ -329,6 +332,8 @@ cp_forward_kernel(const FwdParams<T> p) {
         dv[(size_t)pp * S + q] = tau * a;
       }
     }
+  } else if (p.diag) {
+    // Diagonal steps shared by the batch: computed once per call (p.dg_*).
   } else if (p.norm_bound) {
     T rmax[S], cmax[S];
 #pragma unroll
@@ -522,7 +527,7 @@ cp_forward_kernel(const FwdParams<T> p) {
 #pragma unroll
         for (int q = 0; q < S; ++q) {
           if (!((act >> q) & 1)) continue;
-          const T sg = p.diag ? sv_[(size_t)qp * S + q] : sigma[q];
+          const T sg = p.diag ? (dg ? __ldg(p.dg_sigma + qp) : sv_[(size_t)qp * S + q]) : sigma[q];
           const T raw = lv[q] + sg * (acc[q] - rbs[q]);
           const T nl = i < me ? raw : pmax(raw, zero);
           lv[q] = nl;
@@ -578,15 +583,17 @@ cp_forward_kernel(const FwdParams<T> p) {
           const T c = kQP ? tg[q] : -tg[q];
           const T qj = qv[q];
           T aa, dd;
-          if (kQP && !p.diag) {
-            // proximal_coefficients (kernels.py:68-73) of this iteration's tau:
-            // fixed steps precompute them (kernels.py:236), accelerated steps
-            // recompute them; either way these are the same operations.
-            aa = one / (one + tau_s[q] * qj);
-            dd = tau_s[q] * aa;
+          if (kQP && !pv) {
+            // proximal_coefficients (kernels.py:68-73) of this iteration's tau
+            // (per column with shared diagonal steps): fixed steps precompute
+            // them (kernels.py:236), accelerated steps recompute them; either
+            // way these are the same operations.
+            const T tj = dg ? __ldg(p.dg_tau + pp) : tau_s[q];
+            aa = one / (one + tj * qj);
+            dd = tj * aa;
           } else {
-            aa = pv ? av[js] : a_s[q];
-            dd = pv ? dv[js] : d_s[q];
+            aa = pv ? av[js] : (dg ? __ldg(p.dg_a + pp) : a_s[q]);
+            dd = pv ? dv[js] : (dg ? __ldg(p.dg_d + pp) : d_s[q]);
           }
           const T off = (-dd) * c;
           const T yr = (aa * yo - dd * t[q]) + off;
@@ -851,6 +858,31 @@ __global__ void permute_rows_kernel(const T* src, int64_t src_stride, const int*
   }
 }
 
+// Diagonal steps of shared values, one lane per sliced-ELL line: the per-line
+// |K| sums in the line's entry order, as SellLines::abs_sum does in the solve.
+template <typename T>
+__global__ void diagonal_steps_kernel(const int* ptr, int nsl, const T* vals, T safety, bool rows,
+                                      T* sigma, T* tau, T* a, T* d) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (int)(blockDim.x >> 5) * gridDim.x;
+  for (int sl = (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); sl < nsl; sl += warps) {
+    const int e0 = ptr[sl];
+    const int width = (ptr[sl + 1] - e0) / kC;
+    T acc = T(0);
+    for (int k = 0, e = e0 + lane; k < width; ++k, e += kC) acc = acc + fabs(vals[e]) * T(1);
+    const int pos = sl * kC + lane;
+    const T step = safety / (acc > T(0) ? pmax(acc, T(1e-12)) : T(1));
+    if (rows) {
+      sigma[pos] = step;
+    } else {
+      const T aa = T(1) / (T(1) + step * T(1));
+      tau[pos] = step;
+      a[pos] = aa;
+      d[pos] = step * aa;
+    }
+  }
+}
+
 // Per-sample values in SELL order: out[b * count + e] = values[b * stride + slot[e]].
 template <typename T>
 __global__ void arrange_sample_values_kernel(const T* values, int64_t stride, const int* slot,
@@ -985,6 +1017,19 @@ cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, 
 }
 
 template <typename T>
+cudaError_t diagonal_steps(const SellView& sv, const T* vr, const T* vc, T safety, T* sigma, T* tau,
+                           T* a, T* d, cudaStream_t stream) {
+  const int threads = 256, per_block = threads / 32;
+  if (sv.nsl_r > 0)
+    diagonal_steps_kernel<T><<<(sv.nsl_r + per_block - 1) / per_block, threads, 0, stream>>>(
+        sv.r_ptr, sv.nsl_r, vr, safety, true, sigma, tau, a, d);
+  if (sv.nsl_c > 0)
+    diagonal_steps_kernel<T><<<(sv.nsl_c + per_block - 1) / per_block, threads, 0, stream>>>(
+        sv.c_ptr, sv.nsl_c, vc, safety, false, sigma, tau, a, d);
+  return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t arrange_sample_values(const T* values, int64_t stride, const int* slot, int count,
                                   int64_t batch, T* out, cudaStream_t stream) {
   const int64_t total = batch * (int64_t)count;
@@ -1028,6 +1073,10 @@ template size_t forward_static_smem<double>(int, int);
 template size_t forward_static_smem<float>(int, int);
 template cudaError_t arrange_values<double>(const double*, const int*, int, double*, cudaStream_t);
 template cudaError_t arrange_values<float>(const float*, const int*, int, float*, cudaStream_t);
+template cudaError_t diagonal_steps<double>(const SellView&, const double*, const double*, double,
+                                            double*, double*, double*, double*, cudaStream_t);
+template cudaError_t diagonal_steps<float>(const SellView&, const float*, const float*, float, float*,
+                                           float*, float*, float*, cudaStream_t);
 template cudaError_t arrange_sample_values<double>(const double*, int64_t, const int*, int, int64_t,
                                                    double*, cudaStream_t);
 template cudaError_t arrange_sample_values<float>(const float*, int64_t, const int*, int, int64_t,

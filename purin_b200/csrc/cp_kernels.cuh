@@ -50,6 +50,14 @@ struct FwdParams {
   const T* vc_ps;
   int64_t nnz_r_ps;
   int64_t nnz_c_ps;
+  // Diagonal steps shared by the batch (diagonal preconditioning with shared
+  // values), computed once per call in the internal orders: sigma per row,
+  // tau, a = 1/(1 + tau), d = tau a per column; null when each tile computes
+  // its own steps into shared memory.
+  const T* dg_sigma;
+  const T* dg_tau;
+  const T* dg_a;
+  const T* dg_d;
   // Per-sample inputs permuted into the internal orders (zero at padding positions).
   const T* tgt_i;    // (B, n_pos)
   const T* rhs_i;    // (B, m_pos)
@@ -183,6 +191,12 @@ template <typename T>
 int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, bool qp = false);
 template <typename T>
 cudaError_t arrange_values(const T* values, const int* slot, int count, T* out, cudaStream_t stream);
+// Diagonal steps of values shared by the batch (kernels.py:76-88) in the
+// internal orders: sigma[pos] = s / rowsum|K|, tau[pos] = s / colsum|K|,
+// a = 1/(1 + tau), d = tau a, with the forward kernel's summation order.
+template <typename T>
+cudaError_t diagonal_steps(const SellView& sv, const T* vr, const T* vc, T safety, T* sigma, T* tau,
+                           T* a, T* d, cudaStream_t stream);
 // Per-sample values into SELL order: out[b * count + e] = values[b * stride + slot[e]]
 // (0 for padding) for b < batch.
 template <typename T>

@@ -148,12 +148,19 @@ def test_forward_tile_widths_match_oracle(monkeypatch, samples_per_tile, threads
     np.testing.assert_allclose(got["gap"], out.gap, rtol=rtol, atol=rtol)
 
 
-@pytest.mark.parametrize("index,batch,dtype", [(0, 16, np.float64), (1, 4, np.float64),
-                                               (0, 16, np.float32)])
-def test_public_solve_matches_oracle(index, batch, dtype):
+@pytest.mark.parametrize("index,batch,dtype,overrides", [
+    (0, 16, np.float64, {}), (1, 4, np.float64, {}), (0, 16, np.float32, {}),
+    # Values shared by the batch with diagonal preconditioning: the diagonal
+    # steps are computed once per call into the workspace.
+    (0, 16, np.float64, {"diagonal_preconditioning": True}),
+    (1, 8, np.float32, {"diagonal_preconditioning": True, "accelerated": False}),
+    (0, 16, np.float64, {"diagonal_preconditioning": True, "tolerance": 1e-4,
+                         "max_iterations": 4000})])
+def test_public_solve_matches_oracle(index, batch, dtype, overrides):
     """End to end: torch preprocessing + forward + post-processing kernels."""
     w = make_workload(index, batch)
     cfg = replace(w.config, max_iterations=min(w.config.max_iterations, 300))
+    cfg = replace(cfg, **overrides)
     oracle = OracleLayer(w.problem, cfg, dtype)
     expected, _ = oracle.solve(w.candidates, w.theta)
     tdt = torch.float64 if dtype == np.float64 else torch.float32
