@@ -340,3 +340,31 @@ def test_gmres_budget_of_one_matches_oracle():
     np.testing.assert_allclose(lres, stats["residual"], rtol=1e-9, atol=1e-14)
     for key in ("rhs", "target", "lower", "upper"):
         np.testing.assert_allclose(got[key], want[key], rtol=0, atol=1e-9, err_msg=key)
+
+
+@pytest.mark.parametrize("seed,accelerated,tol", [(1, False, 1e-5), (2, True, 3e-5),
+                                                 (5, False, 1e-5)])
+def test_adjoint_fp32_matches_oracle(seed, accelerated, tol):
+    """fp32 implicit VJP against the fp32 oracle: every cotangent within 1e-4 of
+    the field's largest gradient (the fp32 bar), identical GMRES status codes."""
+    from purin_b200 import ImplicitGradientConfig
+
+    problem, theta, target = _converging_problem(seed, dtype=np.float32)
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=tol, accelerated=accelerated,
+                              linear_solver=LinearSolverConfig(tolerance=1e-5),
+                              implicit_gradient=ImplicitGradientConfig(adjoint_tolerance=1e-4))
+    oracle = OracleLayer(problem, cfg, np.float32)
+    expected, saved = oracle.solve(target, theta)
+    assert expected["gradient_eligible"].any()
+    cot = np.random.default_rng(100 + seed).normal(size=target.shape).astype(np.float32)
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    layer = _layer(problem, cfg, target.shape[0], torch.float32)
+    got, status, _ = boundary_adjoint(layer, oracle, saved, cot)
+    np.testing.assert_array_equal(status, stats["code"])
+    for key in ("values", "rhs", "target", "lower", "upper"):
+        exp = want[key]
+        if key == "values":
+            exp = ell_to_csr(exp, list(oracle.proj.mask.sum(axis=1)))
+        scale = max(float(np.abs(exp).max()), 1e-6)
+        np.testing.assert_allclose(got[key], exp, rtol=0, atol=1e-4 * scale, err_msg=key)

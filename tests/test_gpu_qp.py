@@ -307,3 +307,29 @@ def test_qp_two_nccl_ranks_reproduce_the_full_batch(tmp_path):
     structure, data, cfg, cot = _lockstep_qp_case()
     want = _qp_grads(structure.prepare(batch_size=8, config=cfg), data, cot, DEV)
     np.testing.assert_array_equal(np.load(out), want.cpu().numpy())
+
+
+def test_gradients_fp32_match_oracle():
+    """fp32 QP gradients w.r.t. every field within 1e-4 of each field's largest."""
+    structure, data = random_qp(1, 6, 8, 2, 4, 3, np.float32, converge=True)
+    from purin_b200 import ImplicitGradientConfig
+
+    cfg = ChambollePockConfig(max_iterations=20000, tolerance=1e-5,
+                              linear_solver=LinearSolverConfig(tolerance=1e-5),
+                              implicit_gradient=ImplicitGradientConfig(adjoint_tolerance=1e-4))
+    oracle = OracleDiagonalQP(8, structure.equality_rows, structure.inequality_rows,
+                              oracle_config(cfg))
+    want, saved = oracle.solve(data)
+    assert want["gradient_eligible"].any()
+    cot_y = np.random.default_rng(61).normal(size=data[0].shape).astype(np.float32)
+    g = oracle.vjp(saved["out"], saved["data"], cot_y, None)
+    g["values"] = g["values"] * saved["scale"][:, :, None]
+    g["rhs"] = g["rhs"] * saved["scale"]
+    solver = structure.prepare(batch_size=6, config=cfg, dtype=torch.float32)
+    tensors = [torch.as_tensor(a, device=DEV).requires_grad_(True) for a in data]
+    res = solver.solve(QPData(*tensors))
+    (res.y * torch.as_tensor(cot_y, device=DEV)).sum().backward()
+    for name, t in zip(FIELDS, tensors):
+        scale = max(float(np.abs(g[name]).max()), 1e-6)
+        np.testing.assert_allclose(t.grad.cpu().numpy(), g[name], rtol=0, atol=1e-4 * scale,
+                                   err_msg=name)
