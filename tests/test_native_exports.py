@@ -51,3 +51,25 @@ def test_plan_creation_reports_a_missing_device_or_bad_structure():
     status = lib.purin_cp_plan_create(ctypes.byref(s), ctypes.byref(handle))
     assert status != 0
     assert lib.purin_cp_last_error()
+
+
+def test_binding_constants_match_the_header_enums():
+    """The ctypes binding's op and stage codes are the header's (a mismatch would
+    size workspaces for the wrong computation)."""
+    text = HEADER.read_text()
+    enum = dict((name, int(value)) for name, value in
+                re.findall(r"^\s*(PURIN_(?:CP|QP)_(?:OP|STAGE)_\w+)\s*=\s*(\d+)", text, flags=re.M))
+    expected = {
+        "PURIN_CP_OP_FORWARD": _native.OP_FORWARD,
+        "PURIN_CP_OP_ADJOINT": _native.OP_ADJOINT,
+        "PURIN_QP_OP_FORWARD": _native.QP_OP_FORWARD,
+        "PURIN_QP_OP_ADJOINT": _native.QP_OP_ADJOINT,
+        "PURIN_CP_OP_FORWARD_SAMPLE_VALUES": _native.OP_FORWARD_SAMPLE_VALUES,
+        "PURIN_QP_OP_FORWARD_SAMPLE_VALUES": _native.QP_OP_FORWARD_SAMPLE_VALUES,
+        "PURIN_CP_STAGE_PREPARE": _native.STAGE_PREPARE,
+        "PURIN_CP_STAGE_CYCLE": _native.STAGE_CYCLE,
+        "PURIN_CP_STAGE_FINISH": _native.STAGE_FINISH,
+    }
+    assert enum == expected
+    for name in _native.EXPORTED:
+        assert name in declared_functions()
