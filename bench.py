@@ -89,9 +89,10 @@ def parse_args():
     p.add_argument("--qp-values", default="shared", choices=["shared", "per-sample"],
                    help="qp: one constraint matrix for the batch (a broadcast view) or a "
                         "separate copy per sample (the same values, materialised)")
-    p.add_argument("--problem", default="projection", choices=["projection", "qp"],
+    p.add_argument("--problem", default="projection", choices=["projection", "qp", "dense"],
                    help="qp: configuration 2's structure as a general diagonal QP "
-                        "(PreparedDiagonalQP), fwd + VJP w.r.t. q, c, values, rhs and bounds")
+                        "(PreparedDiagonalQP), fwd + VJP w.r.t. q, c, values, rhs and bounds; "
+                        "dense: solve_dense_implicit on per-sample dense matrices")
     return p.parse_args()
 
 
@@ -428,6 +429,169 @@ def main_qp(args, world, rank, local_rank, device, barrier):
         dist.destroy_process_group()
 
 
+DENSE_METRIC = "dense QP samples/sec at fixed iters (fwd+VJP)"
+DENSE_ITERATIONS = 2000
+
+
+def cpu_baseline_dense(samples):
+    """The NumPy dense-adapter oracle (fwd 2000 iterations + VJP) on a bounded sample."""
+    from oracle.dense import OracleDense  # noqa: E402  (test infrastructure, checker only)
+    from purin_b200.workloads import dense_workload
+
+    q, c, A, b, C, d, lower, upper, targets = dense_workload(samples)
+    oracle = OracleDense(q.shape[1], A.shape[1], C.shape[1], max_iterations=DENSE_ITERATIONS,
+                         tolerance=1e-9)
+    t0 = time.perf_counter()
+    out = oracle.run(q, c, A, b, C, d, lower, upper)
+    oracle.vjp(out, q, c, A, b, C, d, lower, upper, out.y - targets)
+    elapsed = time.perf_counter() - t0
+    return {"value": samples / elapsed, "unit": "samples/s", "cores": 1, "kind": "port",
+            "sample": f"{samples} samples of the dense workload (fwd {DENSE_ITERATIONS} it + "
+                      f"VJP) in {elapsed:.1f} s: the NumPy dense-adapter restatement (oracle/)"}
+
+
+def main_dense(args, world, rank, local_rank, device, barrier):
+    """``--problem dense``: ``solve_dense_implicit`` on per-sample dense matrices."""
+    import torch
+    import torch.distributed as dist
+
+    from purin_b200 import dense_layer
+    from purin_b200.workloads import dense_workload
+
+    batch = args.batch or 16384
+    total = batch * world
+    problem = dense_workload(batch, seed=rank)
+    q, c, A, b, C, d, lower, upper, targets = problem
+    n, me, mi = q.shape[1], A.shape[1], C.shape[1]
+    m = me + mi
+    tol = args.cp_tolerance if args.cp_tolerance is not None else 1e-9
+    dev = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device=device)
+    inputs_d = [dev(x) for x in problem]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    solver_box = {}
+
+    def step(inputs):
+        leaves = [x.detach().requires_grad_(True) for x in inputs[:8]]
+        y, _, _ = dense_layer.solve_dense_implicit(
+            *leaves, tolerance=tol, max_iterations=DENSE_ITERATIONS, backend=str(device))
+        loss = 0.5 * ((y - inputs[8]) ** 2).sum()
+        loss.backward()
+        return loss, leaves
+
+    for _ in range(args.warmup):
+        step(inputs_d)
+    barrier()
+    solver_box["solver"] = next(iter(dense_layer._SOLVERS.values()))  # the one solve shape
+    timers, step_ms, work = [], [], []
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            dense_layer.record_launches(timers)
+            start.record()
+            step(inputs_d)
+            end.record()
+            dense_layer.record_launches(None)
+            torch.cuda.synchronize(device)
+            step_ms.append(start.elapsed_time(end))
+            work.append(sum(solver_box["solver"].last_work))
+        barrier()
+    clock_info = clocks.summary()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(float(sum(step_ms) / len(step_ms)))
+    per_kernel = {}
+    for name, s0, e0 in timers:
+        per_kernel.setdefault(name, []).append(s0.elapsed_time(e0))
+    per_step = lambda name: (sum(per_kernel[name]) / args.steps if name in per_kernel
+                             else float("nan"))
+    fwd_ms, adj_ms = per_step("forward"), per_step("adjoint")
+    launches = count_native_launches(lambda: step(inputs_d), device) * args.steps
+    # Per sample-iteration: read y, ybar, q, c, lambda, rhs and write y, ybar,
+    # lambda ((6n + 3m) * 8 B), and read the sample's own row values twice (row
+    # and column order: 2 * m * n * 8 B).
+    bytes_per_iteration = ((6 * n + 3 * m) + 2 * m * n) * 8
+    fwd_bytes = float(sum(work) / len(work)) * bytes_per_iteration
+    hbm, peak_kind = peaks()
+    achieved = fwd_bytes / (fwd_ms / 1000.0) / 1e9
+
+    # End to end: every input from pinned host memory (the per-sample matrices
+    # included); the loss and the gradients w.r.t. c and A back to pinned host memory.
+    pin = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64).pin_memory()
+    inputs_h = [pin(x) for x in problem]
+    gc_h, gA_h = torch.empty_like(inputs_h[1]).pin_memory(), torch.empty_like(inputs_h[2]).pin_memory()
+    loss_h = torch.empty((), dtype=torch.float64).pin_memory()
+
+    def step_e2e():
+        loss, leaves = step([x.to(device, non_blocking=True) for x in inputs_h])
+        gc_h.copy_(leaves[1].grad, non_blocking=True)
+        gA_h.copy_(leaves[2].grad, non_blocking=True)
+        loss_h.copy_(loss.detach(), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    barrier()
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        step_e2e()
+        end.record()
+        torch.cuda.synchronize(device)
+        e2e_ms.append(start.elapsed_time(end))
+    barrier()
+    e2e = max_over_ranks(float(sum(e2e_ms) / len(e2e_ms)))
+    h2d = sum(x.numel() for x in inputs_h) * 8
+    d2h = (gc_h.numel() + gA_h.numel() + 1) * 8
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_dense(args.cpu_samples or 64)
+    if rank == 0:
+        line = {
+            "metric": DENSE_METRIC, "value": total / (ms / 1000.0), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded dense QPs; no dataset)",
+            "config": {
+                "workload": f"dense: solve_dense_implicit, fp64, n={n}, me={me}, mi={mi}, "
+                            "dense per-sample A and C ~ N(0,1), q~U(0.5,2), c=-q*candidate, "
+                            f"per-sample bounds; at most {DENSE_ITERATIONS} fixed-step CP "
+                            f"iterations (tolerance {tol:g}, batch-wide trip count); loss "
+                            "0.5||y-t||^2, gradients w.r.t. c, A, b, C, d, lower, upper",
+                "samples_per_gpu": batch, "global_batch": total,
+                "l2": "inputs larger than L2 (per-sample matrices) and flushed between "
+                      "timed steps (256 MB write outside the step events)",
+                "sample_iterations_per_step": float(sum(work) / len(work)),
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "cp_forward_kernel<kQP> (per-sample values)",
+                "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None, "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": fwd_bytes, "launch_ms": fwd_ms,
+                "note": "((6n+3m) + 2mn)*8 B per executed sample-iteration",
+            },
+            "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms},
+            "gpu_launches": launches,
+            "e2e": {"value": total / (e2e / 1000.0), "unit": "samples/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e},
+            "clocks": clock_info,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -458,6 +622,9 @@ def main():
 
     if args.problem == "qp":
         main_qp(args, world, rank, local_rank, device, barrier)
+        return
+    if args.problem == "dense":
+        main_dense(args, world, rank, local_rank, device, barrier)
         return
 
     index = args.config

@@ -327,7 +327,18 @@ typedef struct PurinQpForwardArgs {
   void* residual;           /* out (B,)                                      */
   void* gap;                /* out (B,)                                      */
   uint8_t* converged;       /* out (B,)                                      */
+  int32_t flags;            /* 0 for PreparedDiagonalQP; PURIN_QP_* bits for
+                               the dense adapter's variant of sparse_cp     */
 } PurinQpForwardArgs;
+
+/* purin_qp_forward flags: the sparse_cp options the dense adapter
+ * (chambolle_pock/dense.py:37-105, dense_implicit.py:14-54) runs with. */
+#define PURIN_QP_FACTORED_PROXIMAL 1 /* y+ = a ((y - tau K^T l) - tau c) (kernels.py:142-145) */
+#define PURIN_QP_NO_STATIONARITY 2   /* check_stationarity=False                       */
+#define PURIN_QP_NO_FREEZE 4         /* freeze_converged=False: accepted samples keep
+                                        iterating; the caller runs the batch's trip
+                                        count as max_iterations                        */
+#define PURIN_QP_NO_VALIDITY 8       /* no all(q > 0) & all(lower <= upper) mask      */
 
 typedef struct PurinQpAdjointArgs {
   int64_t batch;

@@ -104,8 +104,13 @@ def diagonal_step_sizes(q, values, support, mask, safety):
     return s / column, s / row
 
 
-def cp_step(state, q, c, rhs, lower, upper, mv, tmv, me, tau, sigma, theta, proximal=None):
-    """``kernels.py:91-150`` (non-factored form): one CP update plus extrapolation."""
+def cp_step(state, q, c, rhs, lower, upper, mv, tmv, me, tau, sigma, theta, proximal=None,
+            factored_proximal=False):
+    """``kernels.py:91-150``: one CP update plus extrapolation.
+
+    ``factored_proximal`` is the dense adapter's form (kernels.py:142-149):
+    ``inverse * ((y - tau K^T l) - tau c)`` clipped as ``minimum(maximum(., l), u)``.
+    """
     y, dual, ybar = state
     dtype = y.dtype
     dual_step = sigma[:, None] if sigma.ndim == 1 else sigma
@@ -116,8 +121,13 @@ def cp_step(state, q, c, rhs, lower, upper, mv, tmv, me, tau, sigma, theta, prox
     inverse, dual_weight, offset = (
         proximal_coefficients(q, c, tau) if proximal is None else proximal
     )
-    next_y = inverse * y - dual_weight * tmv(next_dual) + offset
-    next_y = clip(next_y, lower, upper)
+    if factored_proximal:
+        step = tau[:, None] if tau.ndim == 1 else tau
+        next_y = inverse * ((y - step * tmv(next_dual)) - step * c)
+        next_y = np.minimum(np.maximum(next_y, lower), upper)
+    else:
+        next_y = inverse * y - dual_weight * tmv(next_dual) + offset
+        next_y = clip(next_y, lower, upper)
     return next_y, next_dual, next_y + theta[:, None] * (next_y - y)
 
 
@@ -179,7 +189,7 @@ def sparse_cp(q, c, values, rhs, support, mask, me, lower, upper, *, accelerated
               safety=0.95, max_iterations=5000, tolerance=1e-9, norm_iterations=20,
               norm_seed=42, y0=None, dual0=None, freeze_converged=False,
               check_stationarity=False, norm_bound=False, diagonal_preconditioning=False,
-              offset=0, total=None, partitionable=True, trace=None):
+              offset=0, total=None, partitionable=True, trace=None, factored_proximal=False):
     """``kernels.py:178-305``: batched fixed-step or accelerated CP with per-sample freeze."""
     batch, n = q.shape
     dtype = q.dtype
@@ -204,7 +214,7 @@ def sparse_cp(q, c, values, rhs, support, mask, me, lower, upper, *, accelerated
     iteration = 0
     while iteration < max_iterations and not np.all(done):
         ny, nd, nb = cp_step((y, dual, ybar), q, c, rhs, lower, upper, mv, tmv, me, tau,
-                             sigma, theta, proximal=proximal)
+                             sigma, theta, proximal=proximal, factored_proximal=factored_proximal)
         residual, gap = diagnostics(ny, nd, q, c, rhs, lower, upper, mv, tmv, me)
         finite = (np.all(np.isfinite(ny), axis=1) & np.all(np.isfinite(nd), axis=1)
                   & np.isfinite(gap))

@@ -71,7 +71,11 @@ class QpForwardArgs(ctypes.Structure):
                 ("values_stride", c_i64), ("rhs", c_vp), ("lower", c_vp), ("upper", c_vp),
                 ("bounds_stride", c_i64), ("y0", c_vp), ("dual0", c_vp), ("tolerance", c_vp),
                 ("sample_offset", c_i64), ("total_batch", c_i64), ("y", c_vp), ("dual", c_vp),
-                ("iterations", c_vp), ("residual", c_vp), ("gap", c_vp), ("converged", c_vp)]
+                ("iterations", c_vp), ("residual", c_vp), ("gap", c_vp), ("converged", c_vp),
+                ("flags", c_i32)]
+
+
+QP_FACTORED_PROXIMAL, QP_NO_STATIONARITY, QP_NO_FREEZE, QP_NO_VALIDITY = 1, 2, 4, 8
 
 
 class QpAdjointArgs(ctypes.Structure):

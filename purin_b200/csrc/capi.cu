@@ -266,6 +266,7 @@ struct QpInputs {
   const void* q;
   const void* c;
   const void* y0;
+  int32_t flags;
 };
 
 template <typename T>
@@ -352,6 +353,7 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.q_i = q_i;
   p.c_i = c_i;
   p.y0_i = y0_i;
+  p.qp_flags = qp ? qp->flags : 0;
   p.rhs_i = rhs_i;
   p.dual0_i = (dual0_i && plan->info.kept_rows > 0) ? dual0_i : nullptr;
   p.lo_i = lo_i;
@@ -1184,7 +1186,10 @@ int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, c
   a.residual = args->residual;
   a.gap = args->gap;
   a.converged = args->converged;
-  const QpInputs qp{args->q, args->c, args->y0};
+  if (args->flags & ~(PURIN_QP_FACTORED_PROXIMAL | PURIN_QP_NO_STATIONARITY | PURIN_QP_NO_FREEZE |
+                      PURIN_QP_NO_VALIDITY))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown purin_qp_forward flags");
+  const QpInputs qp{args->q, args->c, args->y0, args->flags};
   DeviceGuard guard(plan->info.device);
   if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

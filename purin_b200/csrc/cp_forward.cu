@@ -596,7 +596,10 @@ cp_forward_kernel(const FwdParams<T> p) {
             dd = pv ? dv[js] : (dg ? __ldg(p.dg_d + pp) : d_s[q]);
           }
           const T off = (-dd) * c;
-          const T yr = (aa * yo - dd * t[q]) + off;
+          // factored_proximal (kernels.py:142-145): inverse * ((y - tau t) - tau c).
+          const T yr = (kQP && (p.qp_flags & 1))
+                           ? aa * ((yo - tau_s[q] * t[q]) - tau_s[q] * c)
+                           : (aa * yo - dd * t[q]) + off;
           const T l = lb[q];
           const T u = ub[q];
           const T yn = clip(yr, l, u);
@@ -663,7 +666,8 @@ cp_forward_kernel(const FwdParams<T> p) {
       }
       sc.stat_it[q] = stat;
       sc.fin_it[q] = f;
-      sc.need_c[q] = (sc.active[q] && f && stat <= sc.tol[q]) ? 1 : 0;
+      const bool stat_ok = (kQP && (p.qp_flags & 2)) || stat <= sc.tol[q];
+      sc.need_c[q] = (sc.active[q] && f && stat_ok) ? 1 : 0;
     }
     __syncthreads();
     bool need_gap = last;
@@ -754,8 +758,8 @@ cp_forward_kernel(const FwdParams<T> p) {
         sc.gap_it[q] = gap;
         sc.resb_it[q] = resb;
         sc.fin_it[q] = finite_all ? 1 : 0;
-        sc.need_c[q] =
-            (sc.active[q] && finite_all && resb <= tol && gap <= tol && sc.stat_it[q] <= tol) ? 1 : 0;
+        const bool stat_ok = (kQP && (p.qp_flags & 2)) || sc.stat_it[q] <= tol;
+        sc.need_c[q] = (sc.active[q] && finite_all && resb <= tol && gap <= tol && stat_ok) ? 1 : 0;
       }
       __syncthreads();
 #pragma unroll
@@ -796,16 +800,21 @@ cp_forward_kernel(const FwdParams<T> p) {
         for (int w = 0; w < kWarps; ++w) res = pmax(res, sc.red[w][q][5]);
         const T gap = sc.gap_it[q], stat = sc.stat_it[q];
         const T tol = sc.tol[q];
-        accepted = sc.fin_it[q] && res <= tol && gap <= tol && stat <= tol;
+        // check_stationarity off (kernels.py:276-277,300-304): acceptance and the
+        // reported residual leave stationarity out.
+        const bool no_stat = kQP && (p.qp_flags & 2);
+        accepted = sc.fin_it[q] && res <= tol && gap <= tol && (no_stat || stat <= tol);
         if (sc.active[q]) {
-          sc.res_out[q] = pmax(res, stat);
+          sc.res_out[q] = no_stat ? res : pmax(res, stat);
           sc.gap_out[q] = gap;
         }
       }
       if (sc.active[q]) {
         sc.count[q] += 1;
         sc.conv[q] = accepted ? 1 : 0;
-        if (accepted) sc.active[q] = 0;
+        // freeze_converged off: an accepted sample keeps iterating (the caller
+        // runs the batch's trip count; kernels.py:266-271).
+        if (accepted && !(kQP && (p.qp_flags & 4))) sc.active[q] = 0;
       }
       if (p.accelerated) {
         const T tau = sc.tau[q];
@@ -838,7 +847,8 @@ cp_forward_kernel(const FwdParams<T> p) {
       p.it_out[b] = sc.count[q];
       p.res_out[b] = sc.res_out[q];
       p.gap_out[b] = sc.gap_out[q];
-      const bool feas = (p.feasible ? (p.feasible[b] != 0) : true) && (!kQP || sc.valid[q]);
+      const bool feas = (p.feasible ? (p.feasible[b] != 0) : true) &&
+                        (!kQP || (p.qp_flags & 8) || sc.valid[q]);
       p.conv_out[b] = (sc.conv[q] && feas) ? 1 : 0;
     }
   }

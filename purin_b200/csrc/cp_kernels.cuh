@@ -71,6 +71,10 @@ struct FwdParams {
   const T* q_i;
   const T* c_i;
   const T* y0_i;
+  // Variants of sparse_cp the dense adapter uses (kQP kernels only; zero for
+  // the projection and the diagonal QP): PURIN_QP_FACTORED_PROXIMAL,
+  // PURIN_QP_NO_STATIONARITY, PURIN_QP_NO_FREEZE, PURIN_QP_NO_VALIDITY bits.
+  int qp_flags;
 };
 
 template <typename T>

@@ -202,3 +202,25 @@ def qp_workload(batch: int, *, seed: int = 0):
     structure = QPStructure(n, tuple(rows[:me]), tuple(rows[me:]))
     values = np.concatenate([A_eq.data, A_in.data]).reshape(1, me + mi, k)
     return structure, q, c, values, rhs, lower, upper, targets
+
+def dense_workload(batch: int, *, seed: int = 0, n: int = 64, me: int = 8, mi: int = 32):
+    """Batched dense diagonal QPs for ``solve_dense_implicit`` (per-sample matrices).
+
+    Per sample: A ~ N(0,1)^(me x n), C ~ N(0,1)^(mi x n), q ~ U(0.5, 2)^n,
+    c = -q * candidate (candidate 2 N(0,1)), b = A x0 and d = C x0 + slack for a
+    seeded x0 ~ U(-0.5, 0.5)^n and slack ~ U(0, 0.1), bounds l ~ U(-2, -0.5),
+    u ~ U(0.5, 2), and a loss target t ~ N(0,1)^n.  Returns
+    (q, c, A, b, C, d, lower, upper, targets) as NumPy float64 arrays.
+    """
+    rng = np.random.default_rng(seed)
+    A = rng.normal(size=(batch, me, n))
+    C = rng.normal(size=(batch, mi, n))
+    x0 = rng.uniform(-0.5, 0.5, (batch, n))
+    b = np.einsum("bmn,bn->bm", A, x0)
+    d = np.einsum("bmn,bn->bm", C, x0) + rng.uniform(0.0, 0.1, (batch, mi))
+    q = rng.uniform(0.5, 2.0, (batch, n))
+    c = -q * (2.0 * rng.normal(size=(batch, n)))
+    lower = rng.uniform(-2.0, -0.5, (batch, n))
+    upper = rng.uniform(0.5, 2.0, (batch, n))
+    targets = rng.normal(size=(batch, n))
+    return q, c, A, b, C, d, lower, upper, targets

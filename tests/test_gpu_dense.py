@@ -1,0 +1,182 @@
+"""Dense / packed CP adapter (``solve_dense_implicit``) on the GPU.
+
+* The reference's analytic cases (PURIN tests/test_dense_cp.py:20-78): value,
+  warm start and the implicit Jacobian dy/dc at 1e-6, with and without Ruiz
+  equilibration and acceleration; no constraint rows.
+* Random dense and packed problems against the oracle (oracle/dense.py):
+  forward at a fixed iteration count and converged with the batch-wide trip
+  count, and the implicit gradients of every input.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.dense import OracleDense
+from purin_b200.dense_layer import solve_dense_implicit
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+JACOBIAN = -np.diag([0.5, 0.25]) + np.outer([0.5, 0.25], [0.5, 0.25]) / 0.75
+
+
+def _equality_qp(dtype=torch.float64):
+    t = lambda x: torch.tensor(x, dtype=dtype, device=DEV)
+    return (t([[2.0, 4.0]]), t([[-2.0, -4.0]]), torch.ones((1, 1, 2), dtype=dtype, device=DEV),
+            torch.ones((1, 1), dtype=dtype, device=DEV), t([[[-1.0, 0.0]]]),
+            torch.zeros((1, 1), dtype=dtype, device=DEV),
+            torch.zeros((1, 2), dtype=dtype, device=DEV),
+            torch.ones((1, 2), dtype=dtype, device=DEV) * 2)
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+@pytest.mark.parametrize("equilibrate", [False, True])
+def test_dense_analytic_equality_qp(accelerated, equilibrate):
+    q, c, A, b, C, d, lo, hi = args = _equality_qp()
+    kwargs = dict(accelerated=accelerated, equilibrate=equilibrate, tolerance=1e-13,
+                  max_iterations=20000)
+    y, eq, iq = solve_dense_implicit(*args, **kwargs)
+    np.testing.assert_allclose(y.cpu().numpy(), [[1 / 3, 2 / 3]], atol=1e-6)
+    warm = solve_dense_implicit(*args, y0=y, lambda0=eq, mu0=iq, **kwargs)[0]
+    np.testing.assert_allclose(warm.cpu().numpy(), y.cpu().numpy(), atol=1e-6)
+    jac = torch.autograd.functional.jacobian(
+        lambda linear: solve_dense_implicit(q, linear[None], A, b, C, d, lo, hi, **kwargs)[0][0],
+        c[0])
+    np.testing.assert_allclose(jac.cpu().numpy(), JACOBIAN, atol=1e-6)
+    # Equality residual and primal feasibility of the reported solution.
+    assert abs(float(y.sum()) - 1.0) < 1e-7
+    assert float(eq.abs().max()) > 0.0
+
+
+def test_dense_analytic_float32():
+    y, _, _ = solve_dense_implicit(*_equality_qp(torch.float32), tolerance=1e-6,
+                                   max_iterations=20000)
+    assert y.dtype == torch.float32
+    np.testing.assert_allclose(y.cpu().numpy(), [[1 / 3, 2 / 3]], atol=1e-4)
+
+
+def test_dense_empty_constraints():
+    q = torch.ones((1, 2), dtype=torch.float64, device=DEV)
+    c = torch.tensor([[-1.0, -2.0]], dtype=torch.float64, device=DEV)
+    empty = torch.zeros((1, 0, 2), dtype=torch.float64, device=DEV)
+    none = torch.zeros((1, 0), dtype=torch.float64, device=DEV)
+    y, eq, iq = solve_dense_implicit(q, c, empty, none, empty, none, torch.zeros_like(q),
+                                     torch.ones_like(q) * 3, equilibrate=True, tolerance=1e-14)
+    np.testing.assert_allclose(y.cpu().numpy(), [[1.0, 2.0]], atol=1e-6)
+    assert eq.shape == (1, 0) and iq.shape == (1, 0)
+
+
+def test_dense_invalid_support_raises():
+    args = _equality_qp()
+    with pytest.raises(ValueError):
+        solve_dense_implicit(*args, inequality_support=((0,), (1,)))  # two rows for one
+    with pytest.raises(ValueError):
+        solve_dense_implicit(*args, inequality_support=((2,),))  # column out of range
+    with pytest.raises(ValueError):
+        solve_dense_implicit(*args, inequality_support=((0, 0),))  # duplicate column
+    with pytest.raises(ValueError):
+        solve_dense_implicit(args[0][0], *args[1:])  # q without a batch axis
+
+
+def _random_dense(batch, n, me, mi, seed, *, support=None):
+    rng = np.random.default_rng(seed)
+    q = rng.uniform(0.5, 2.0, (batch, n))
+    q[0] *= 4.0  # spread the samples' iteration counts
+    c = rng.normal(size=(batch, n))
+    A = rng.normal(size=(batch, me, n))
+    C = rng.normal(size=(batch, mi, n))
+    if support is not None:
+        keep = np.zeros((mi, n), dtype=bool)
+        for i, row in enumerate(support):
+            keep[i, list(row)] = True
+        C = np.where(keep[None], C, 0.0)
+    y_feasible = rng.uniform(-0.5, 0.5, (batch, n))
+    b = np.einsum("bmn,bn->bm", A, y_feasible)
+    d = np.einsum("bmn,bn->bm", C, y_feasible) + rng.uniform(0.0, 0.5, (batch, mi))
+    return q, c, A, b, C, d, -np.ones((batch, n)), np.ones((batch, n))
+
+
+SUPPORT = ((0, 2, 5), (1, 3), (4, 6, 7, 0), (2,))
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+@pytest.mark.parametrize("packed", [False, True])
+def test_dense_parity_fixed_iterations(accelerated, packed):
+    """200 iterations (no sample accepted): every output against the oracle."""
+    support = SUPPORT if packed else None
+    problem = _random_dense(5, 8, 2, 4, seed=11, support=support)
+    oracle = OracleDense(8, 2, 4, inequality_support=support, accelerated=accelerated,
+                         tolerance=1e-300, max_iterations=200)
+    ref = oracle.solve(*problem)
+    got = solve_dense_implicit(*(torch.as_tensor(x, device=DEV) for x in problem),
+                               accelerated=accelerated, tolerance=1e-300, max_iterations=200,
+                               inequality_support=support, return_iterations=True)
+    for g, r in zip(got[:3], ref[:3]):
+        np.testing.assert_allclose(g.cpu().numpy(), r, rtol=1e-9, atol=1e-12)
+    assert got[3].cpu().tolist() == [200] * 5
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+@pytest.mark.parametrize("equilibrate", [False, True])
+def test_dense_parity_trip_count(accelerated, equilibrate):
+    """Converged solve: every sample runs the batch's trip count, as in the shared loop."""
+    problem = _random_dense(4, 6, 2, 3, seed=3)
+    oracle = OracleDense(6, 2, 3, accelerated=accelerated, tolerance=1e-8, max_iterations=4000)
+    ref = oracle.solve(*problem, equilibrate=equilibrate)
+    got = solve_dense_implicit(*(torch.as_tensor(x, device=DEV) for x in problem),
+                               accelerated=accelerated, tolerance=1e-8, max_iterations=4000,
+                               equilibrate=equilibrate, return_iterations=True)
+    trips = int(ref[3][0])
+    assert trips < 4000 and set(ref[3].tolist()) == {trips}
+    assert got[3].cpu().tolist() == ref[3].tolist()
+    for g, r in zip(got[:3], ref[:3]):
+        np.testing.assert_allclose(g.cpu().numpy(), r, rtol=1e-9, atol=1e-11)
+
+
+def test_dense_shared_matrices_match_per_sample():
+    """A 2-D constraint matrix (one copy for the batch) gives the 3-D result."""
+    q, c, A, b, C, d, lo, hi = _random_dense(3, 6, 2, 3, seed=5)
+    A = np.broadcast_to(A[:1], A.shape)
+    C = np.broadcast_to(C[:1], C.shape)
+    t = lambda x: torch.as_tensor(np.array(x), device=DEV)
+    per = solve_dense_implicit(t(q), t(c), t(A), t(b), t(C), t(d), t(lo), t(hi), tolerance=1e-9,
+                               max_iterations=4000)
+    one = solve_dense_implicit(t(q), t(c), t(A[0]), t(b), t(C[0]), t(d), t(lo), t(hi),
+                               tolerance=1e-9, max_iterations=4000)
+    for g, r in zip(one, per):
+        torch.testing.assert_close(g, r, rtol=1e-12, atol=1e-14)
+    # Gradients of the shared matrix sum the per-sample ones.
+    A1 = t(A[0]).requires_grad_()
+    A3 = t(A).requires_grad_()
+    solve_dense_implicit(t(q), t(c), A1, t(b), t(C[0]), t(d), t(lo), t(hi), tolerance=1e-9,
+                         max_iterations=4000)[0].sum().backward()
+    solve_dense_implicit(t(q), t(c), A3, t(b), t(C), t(d), t(lo), t(hi), tolerance=1e-9,
+                         max_iterations=4000)[0].sum().backward()
+    torch.testing.assert_close(A1.grad, A3.grad.sum(dim=0), rtol=1e-9, atol=1e-11)
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+def test_dense_gradients_match_oracle(accelerated):
+    """Implicit cotangents of c, A, b, C, d and the bounds; q gets none (frozen proximal)."""
+    problem = _random_dense(4, 6, 2, 3, seed=8)
+    oracle = OracleDense(6, 2, 3, accelerated=accelerated, tolerance=1e-10, max_iterations=8000)
+    inputs = [torch.as_tensor(x, device=DEV).requires_grad_() for x in problem]
+    y, eq, iq = solve_dense_implicit(*inputs, accelerated=accelerated, tolerance=1e-10,
+                                     max_iterations=8000)
+    rng = np.random.default_rng(1)
+    wy, weq, wiq = rng.normal(size=(4, 6)), rng.normal(size=(4, 2)), rng.normal(size=(4, 3))
+    loss = ((y * torch.as_tensor(wy, device=DEV)).sum()
+            + (eq * torch.as_tensor(weq, device=DEV)).sum()
+            + (iq * torch.as_tensor(wiq, device=DEV)).sum())
+    loss.backward()
+    out = oracle.run(*problem)
+    grads = oracle.vjp(out, *problem, wy, np.concatenate((weq, wiq), axis=1))
+    gq, gc, gA, gb, gC, gd, glo, ghi = (x.grad.cpu().numpy() for x in inputs)
+    expect = dict(q=(gq, grads["q"]), c=(gc, grads["c"]),
+                  A=(gA, grads["values"][:, :2]), C=(gC, grads["values"][:, 2:]),
+                  b=(gb, grads["rhs"][:, :2]), d=(gd, grads["rhs"][:, 2:]),
+                  lower=(glo, grads["lower"]), upper=(ghi, grads["upper"]))
+    for name, (g, r) in expect.items():
+        np.testing.assert_allclose(g, r, rtol=1e-7, atol=1e-9, err_msg=name)
+    assert np.all(gq == 0.0)
