@@ -170,11 +170,18 @@ def count_native_launches(step, device):
     from torch.profiler import ProfilerActivity, profile
 
     torch.cuda.synchronize(device)
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        step()
-        torch.cuda.synchronize(device)
-    return sum(1 for e in prof.events()
-               if e.device_type == torch.autograd.DeviceType.CUDA and "purin::" in e.name)
+    count = 0
+    # The profiler's first capture in a process can come back without device
+    # events; a step always launches this library's kernels, so retry.
+    for _ in range(3):
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize(device)
+        count = sum(1 for e in prof.events()
+                    if e.device_type == torch.autograd.DeviceType.CUDA and "purin::" in e.name)
+        if count:
+            break
+    return count
 
 
 def _native_oracle(workload, threads):

@@ -120,22 +120,28 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
-  // fits, PURIN_CP_TILE_THREADS (256, 512 or 1024) the threads per CTA.
+  // fits, PURIN_CP_TILE_THREADS (256, 512 or 1024; 128 for QP plans) the
+  // threads per CTA.
   int forced = 0, forced_threads = 0;
   if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
   if (const char* env = std::getenv("PURIN_CP_TILE_THREADS")) forced_threads = std::atoi(env);
   // Default: the shape whose resident CTAs hold the most warps over the batch
   // (the iteration is latency-bound), then the most samples, then the first of
   // this list.  Every shape whose state fits in shared memory is a candidate.
-  static const int kShapes[6][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
+  static const int kShapes[7][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
                                     {4, purin::kForwardThreads}, {8, purin::kForwardThreads},
-                                    {1, 2 * purin::kForwardThreads}, {1, purin::kWideThreads}};
+                                    {1, 2 * purin::kForwardThreads}, {1, purin::kWideThreads},
+                                    {1, purin::kNarrowThreads}};
+  // The narrow QP tile only where a sample's vectors give its 128 threads at
+  // most 4 entries each: larger samples keep the 256-thread tile's parallelism.
+  const bool narrow_ok = qp && (int64_t)n_pos + m_pos <= 4 * purin::kNarrowThreads;
   int best = -1;
   int64_t best_warps = -1, best_samples = -1;
   int pair_blocks = 0;  // resident CTAs per SM of the two-sample 256-thread tile (shape 1)
-  for (int k = 0; k < 6; ++k) {
+  for (int k = 0; k < 7; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
     if (qp && S != 1) continue;  // the QP kernels are built for one-sample tiles
+    if (NT == purin::kNarrowThreads && !(narrow_ok || (qp && forced_threads == NT))) continue;
     const size_t stat = f64 ? purin::forward_static_smem<double>(S, NT)
                             : purin::forward_static_smem<float>(S, NT);
     // Shared-memory tiles read the 16-bit index pairs (always present when a

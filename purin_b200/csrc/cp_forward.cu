@@ -243,10 +243,10 @@ __device__ __forceinline__ T dual_minimiser(T tt, T qj, T l, T u) {
 }
 
 // Resident CTAs per SM the register budget is sized for (64 registers per
-// thread for one-sample tiles): 1 x 1024, 2 x 512, or 4 / 2 / 1 CTAs of 256
-// threads for S = 1 / 2 / wider.
+// thread for one-sample tiles): 1 x 1024, 2 x 512, 8 x 128, or 4 / 2 / 1 CTAs
+// of 256 threads for S = 1 / 2 / wider.
 constexpr int forward_min_blocks(int S, int NT) {
-  return NT >= 1024 ? 1 : NT >= 512 ? 2 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
+  return NT >= 1024 ? 1 : NT >= 512 ? 2 : NT <= 128 ? 8 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
 }
 
 template <typename T, int S, int NT, bool kSmem, bool kShared, bool kQP>
@@ -937,10 +937,17 @@ cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaSt
 
 // Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads, and S = 1
 // with 2 or 4 times as many threads for shared-memory tiles of one sample.
-// The diagonal QP is built for the one-sample shapes only.
+// The diagonal QP is built for the one-sample shapes only, plus one-sample
+// tiles of kNarrowThreads threads.
 template <typename T, bool kShared, bool kQP>
 cudaError_t launch_shared(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                           cudaStream_t stream) {
+  if constexpr (kQP) {
+    if (NT == kNarrowThreads)
+      return S == 1 && smem ? launch_s<T, 1, kNarrowThreads, kShared, true>(p, smem, smem_bytes,
+                                                                            stream)
+                            : cudaErrorInvalidValue;
+  }
   if (NT == 2 * kForwardThreads)
     return S == 1 ? launch_s<T, 1, 2 * kForwardThreads, kShared, kQP>(p, smem, smem_bytes, stream)
                   : cudaErrorInvalidValue;
@@ -976,6 +983,10 @@ int blocks_per_sm_s(size_t smem_bytes) {
 
 template <typename T, bool kShared, bool kQP>
 int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
+  if constexpr (kQP) {
+    if (NT == kNarrowThreads)
+      return S == 1 ? blocks_per_sm_s<T, 1, kNarrowThreads, kShared, true>(smem_bytes) : 0;
+  }
   if (NT == 2 * kForwardThreads)
     return S == 1 ? blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared, kQP>(smem_bytes) : 0;
   if (NT == kWideThreads)
@@ -1007,6 +1018,7 @@ int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, 
 
 template <typename T>
 size_t forward_static_smem(int S, int NT) {
+  if (NT == kNarrowThreads) return sizeof(TileScratch<T, 1, kNarrowThreads / 32>);
   if (NT == 2 * kForwardThreads) return sizeof(TileScratch<T, 1, 2 * kForwardThreads / 32>);
   if (NT == kWideThreads) return sizeof(TileScratch<T, 1, kWideThreads / 32>);
   switch (S) {

@@ -180,6 +180,9 @@ struct PostParams {
 // or two CTAs of kForwardThreads per SM run 2 x or 4 x (kWideThreads) as many.
 constexpr int kForwardThreads = 256;
 constexpr int kWideThreads = 1024;
+// One-sample QP tiles of small problems (a few hundred variables and rows): half
+// the threads, twice the resident samples per SM at the same register budget.
+constexpr int kNarrowThreads = 128;
 
 // S samples per tile, NT threads per CTA; smem: the tile state lives in shared
 // memory (smem_bytes of it).

@@ -180,3 +180,32 @@ def test_dense_gradients_match_oracle(accelerated):
     for name, (g, r) in expect.items():
         np.testing.assert_allclose(g, r, rtol=1e-7, atol=1e-9, err_msg=name)
     assert np.all(gq == 0.0)
+
+
+@pytest.mark.parametrize("case", ["equality_only_unbounded", "inequality_only_packed",
+                                  "max_iterations_reached"])
+def test_dense_edge_cases_match_oracle(case):
+    """Zero-width blocks, infinite bounds, and a trip count capped by max_iterations."""
+    support = None
+    max_iterations, tolerance = 4000, 1e-9
+    if case == "equality_only_unbounded":
+        q, c, A, b, C, d, lo, hi = _random_dense(3, 6, 3, 0, seed=21)
+        lo, hi = np.full_like(lo, -np.inf), np.full_like(hi, np.inf)
+    elif case == "inequality_only_packed":
+        support = SUPPORT
+        q, c, A, b, C, d, lo, hi = _random_dense(3, 8, 0, 4, seed=22, support=support)
+    else:
+        q, c, A, b, C, d, lo, hi = _random_dense(4, 6, 2, 3, seed=23)
+        max_iterations = 180  # first acceptances 141, 149, 220, 199: two samples accept
+    problem = (q, c, A, b, C, d, lo, hi)
+    oracle = OracleDense(q.shape[1], A.shape[1], C.shape[1], inequality_support=support,
+                         tolerance=tolerance, max_iterations=max_iterations)
+    ref = oracle.solve(*problem)
+    got = solve_dense_implicit(*(torch.as_tensor(x, device=DEV) for x in problem),
+                               tolerance=tolerance, max_iterations=max_iterations,
+                               inequality_support=support, return_iterations=True)
+    assert got[3].cpu().tolist() == ref[3].tolist()
+    for g, r in zip(got[:3], ref[:3]):
+        np.testing.assert_allclose(g.cpu().numpy(), r, rtol=1e-9, atol=1e-11)
+    if case == "max_iterations_reached":
+        assert ref[3].tolist() == [180] * 4
