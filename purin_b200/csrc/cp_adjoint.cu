@@ -32,6 +32,8 @@
 // workspace (x, thresholds, residuals, linearisation codes).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "cp_kernels.cuh"
 
@@ -39,8 +41,15 @@ namespace purin {
 
 namespace {
 
+// Threads per CTA: at most kThreads (the shared reduction arrays are sized for
+// it); every loop and reduction uses blockDim.x, so a launch may use fewer.
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+// Krylov vectors of at most this many entries per thread run on kSmallThreads:
+// a small sample gets half the threads and an SM twice the samples in flight
+// at the same register budget (the per-sample phases are barrier-bound).
+constexpr int kSmallThreads = 128;
+constexpr int kSmallEntriesPerThread = 4;
 constexpr int kChunk = 8;  // basis vectors per register-resident dot-product chunk
 
 template <typename T>
@@ -65,7 +74,7 @@ __device__ T block_sum(T v, T* red) {
   __syncthreads();
   T total = T(0);
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) total = total + red[w];
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total = total + red[w];
   __syncthreads();
   return total;
 }
@@ -77,7 +86,7 @@ __device__ T block_max(T v, T* red) {
   __syncthreads();
   T total = T(0);
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) total = pmax(total, red[w]);
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total = pmax(total, red[w]);
   __syncthreads();
   return total;
 }
@@ -91,7 +100,7 @@ __device__ T block_max_from(T v, T* red) {
   __syncthreads();
   T total = red[0];
 #pragma unroll
-  for (int w = 1; w < kWarps; ++w) total = pmax(total, red[w]);
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) total = pmax(total, red[w]);
   __syncthreads();
   return total;
 }
@@ -163,7 +172,7 @@ __device__ void apply_operator(const DevStructure& st, const Sample<T>& s, T* bu
   T* zy = buf;
   T* zd = buf + n;
   T* zb = buf + n + m;
-  for (int j = threadIdx.x; j < n; j += kThreads) {
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
     const T vy = zy[j], vb = zb[j];
     const T gg = (vy + vb) + vb;
     const T graw = gg * code_factor<T>(s.yc[j] & 3);
@@ -173,7 +182,7 @@ __device__ void apply_operator(const DevStructure& st, const Sample<T>& s, T* bu
     zy[j] = vy - (aa * graw - vb);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < m; i += kThreads) {
+  for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
     T acc = T(0);
     for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * tn[st.col[k]];
     const T mu = zd[i] + acc;
@@ -183,7 +192,7 @@ __device__ void apply_operator(const DevStructure& st, const Sample<T>& s, T* bu
     zd[i] = zd[i] - mur;
   }
   __syncthreads();
-  for (int j = threadIdx.x; j < n; j += kThreads) {
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
     T acc = T(0);
     for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
       acc = acc + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
@@ -209,7 +218,7 @@ __device__ void basis_dots(const T* V, int W, const T* buf, int r, T* out, T* re
 #pragma unroll
     for (int q = 0; q < kChunk; ++q) part[q] = T(0);
 #pragma unroll 2
-    for (int e = threadIdx.x; e < W; e += kThreads) {
+    for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
       const T be = buf[e];
       T v[kChunk];
 #pragma unroll
@@ -228,7 +237,7 @@ __device__ void basis_dots(const T* V, int W, const T* buf, int r, T* out, T* re
     __syncthreads();
     if (threadIdx.x < kChunk && c0 + (int)threadIdx.x < r) {
       T total = T(0);
-      for (int w = 0; w < kWarps; ++w) total = total + red[w * kChunk + threadIdx.x];
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total = total + red[w * kChunk + threadIdx.x];
       out[c0 + threadIdx.x] = total;
     }
     __syncthreads();
@@ -255,7 +264,7 @@ __device__ __forceinline__ T basis_combination(const T* V, int W, int e, int r, 
 template <typename T>
 __device__ void basis_update(const T* V, int W, T* buf, int r, const T* c) {
 #pragma unroll 2
-  for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = buf[e] - basis_combination(V, W, e, r, c);
+  for (int e = threadIdx.x; e < W; e += (int)blockDim.x) buf[e] = buf[e] - basis_combination(V, W, e, r, c);
   __syncthreads();
 }
 
@@ -278,10 +287,10 @@ template <typename T>
 __device__ void qp_steps(const AdjParams<T>& p, int64_t X, const T* qx, T* base, T L, T* red) {
   const int n = p.st.n, m = p.st.m;
   T qmax = T(-INFINITY);
-  for (int j = threadIdx.x; j < n; j += kThreads) qmax = pmax(qmax, qx[j]);
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) qmax = pmax(qmax, qx[j]);
   qmax = block_max_from(qmax, red);
   const T tau = p.safety / (qmax + L);
-  for (int j = threadIdx.x; j < n; j += kThreads) {
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
     const T a = T(1) / (T(1) + tau * qx[j]);
     base[j] = a;
     base[n + j] = tau * a;
@@ -346,12 +355,12 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     const T* qx = p.qp ? p.q + X * n : nullptr;
     T* base = (p.diag || p.qp) ? p.dsteps + X * ((p.qp ? 3 : 2) * (int64_t)n + m) : nullptr;
     if (p.diag) {
-      for (int i = threadIdx.x; i < m; i += kThreads) {
+      for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
         T acc = zero;
         for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + fabs(vals[k]) * one;
         base[2 * n + i] = p.safety / (acc > zero ? pmax(acc, T(1e-12)) : one);
       }
-      for (int j = threadIdx.x; j < n; j += kThreads) {
+      for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
         T acc = zero;
         for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
           acc = acc + fabs(vals[st.csc_slot[e]]) * one;
@@ -364,12 +373,12 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     } else if (p.qp && p.norm_bound) {
       // L = sqrt(max row sum |K| * max column sum |K|) (diagonal_qp.py:143-148).
       T rmax = zero, cmax = zero;
-      for (int i = threadIdx.x; i < m; i += kThreads) {
+      for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
         T acc = zero;
         for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + fabs(vals[k]) * one;
         rmax = pmax(rmax, acc);
       }
-      for (int j = threadIdx.x; j < n; j += kThreads) {
+      for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
         T acc = zero;
         for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
           acc = acc + fabs(vals[st.csc_slot[e]]) * one;
@@ -384,24 +393,24 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       split_key(p.norm_seed, p.sample_offset + X, p.total_batch, p.partitionable != 0, k0, k1);
       T* x = buf;
       T ss = zero;
-      for (int j = threadIdx.x; j < n; j += kThreads) {
+      for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
         const T v = NormalBits<T>::draw(k0, k1, j, n, p.partitionable != 0);
         x[j] = v;
         ss = ss + v * v;
       }
       const T nrm = sqrt(block_sum(ss, red)) + T(1e-12);
-      for (int j = threadIdx.x; j < n; j += kThreads) x[j] = x[j] / nrm;
+      for (int j = threadIdx.x; j < n; j += (int)blockDim.x) x[j] = x[j] / nrm;
       T eig = zero;
       for (int it = 0; it < p.norm_iterations; ++it) {
         __syncthreads();
-        for (int i = threadIdx.x; i < m; i += kThreads) {
+        for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
           T acc = zero;
           for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + vals[k] * x[st.col[k]];
           tm[i] = acc;
         }
         __syncthreads();
         T xz = zero, zz = zero;
-        for (int j = threadIdx.x; j < n; j += kThreads) {
+        for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
           T acc = zero;
           for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
             acc = acc + vals[st.csc_slot[e]] * tm[st.csc_row[e]];
@@ -411,7 +420,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         }
         eig = block_sum(xz, red);
         const T zn = sqrt(block_sum(zz, red)) + T(1e-12);
-        for (int j = threadIdx.x; j < n; j += kThreads) x[j] = tn[j] / zn;
+        for (int j = threadIdx.x; j < n; j += (int)blockDim.x) x[j] = tn[j] / zn;
       }
       const T L = pmax(sqrt(pmax(eig, zero)) + T(1e-12), T(1e-12));
       if (p.qp) {
@@ -424,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     __syncthreads();
     const Sample<T> s = make_sample(p, X);
     // Linearisation point (y*, lambda*, ybar = y*): lambda+ and derivative codes.
-    for (int i = threadIdx.x; i < m; i += kThreads) {
+    for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
       T acc = zero;
       for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * s.ys[st.col[k]];
       const T sg = s.sv ? s.sv[i] : s.sigma;
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       s.lamp[i] = lp;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < n; j += kThreads) {
+    for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
       T t = zero;
       for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
         t = t + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
@@ -456,7 +465,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     __syncthreads();
     // Right-hand side scale, threshold, x = 0 and the initial residual.
     T gmax = zero;
-    for (int e = threadIdx.x; e < W; e += kThreads) {
+    for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
       gmax = pmax(gmax, fabs(rhs_entry(s, n, m, e)));
       buf[e] = zero;
       p.x[X * W + e] = zero;
@@ -464,7 +473,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     gmax = block_max(gmax, red);
     apply_operator(st, s, buf, tn, tm);
     T r0 = zero;
-    for (int e = threadIdx.x; e < W; e += kThreads) r0 = pmax(r0, fabs(rhs_entry(s, n, m, e) - buf[e]));
+    for (int e = threadIdx.x; e < W; e += (int)blockDim.x) r0 = pmax(r0, fabs(rhs_entry(s, n, m, e) - buf[e]));
     r0 = block_max(r0, red);
     if (threadIdx.x == 0) {
       const T thr = pmax(p.lin_atol, p.lin_tol * gmax);
@@ -495,25 +504,25 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       const Sample<T> s = make_sample(p, X);
       T* x = p.x + X * W;
       // residual = g - A x, normalised into V[0]
-      for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = x[e];
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) buf[e] = x[e];
       __syncthreads();
       apply_operator(st, s, buf, tn, tm);
       T ss = zero;
-      for (int e = threadIdx.x; e < W; e += kThreads) {
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
         const T r = rhs_entry(s, n, m, e) - buf[e];
         buf[e] = r;
         ss = ss + r * r;
       }
       const T beta = sqrt(block_sum(ss, red));
       const T safe_beta = pmax(beta, eps);
-      for (int e = threadIdx.x; e < W; e += kThreads) {
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
         const T v = buf[e] / safe_beta;
         buf[e] = v;
         V[e] = v;
       }
-      for (int q = threadIdx.x; q < (R + 1) * R; q += kThreads) hess[q] = zero;
-      for (int q = threadIdx.x; q < R + 1; q += kThreads) proj[q] = q == 0 ? beta : zero;
-      for (int q = threadIdx.x; q < R; q += kThreads) { cs[q] = zero; sn[q] = zero; }
+      for (int q = threadIdx.x; q < (R + 1) * R; q += (int)blockDim.x) hess[q] = zero;
+      for (int q = threadIdx.x; q < R + 1; q += (int)blockDim.x) proj[q] = q == 0 ? beta : zero;
+      for (int q = threadIdx.x; q < R; q += (int)blockDim.x) { cs[q] = zero; sn[q] = zero; }
       if (threadIdx.x == 0) s_flag = 1;
       __syncthreads();
       int it = 0;
@@ -523,14 +532,14 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         basis_update(V, W, buf, it + 1, coef);
         basis_dots(V, W, buf, it + 1, c2, red);
         basis_update(V, W, buf, it + 1, c2);
-        if (threadIdx.x <= it) coef[threadIdx.x] = coef[threadIdx.x] + c2[threadIdx.x];
+        for (int q = threadIdx.x; q <= it; q += (int)blockDim.x) coef[q] = coef[q] + c2[q];
         T nsq = zero;
-        for (int e = threadIdx.x; e < W; e += kThreads) nsq = nsq + buf[e] * buf[e];
+        for (int e = threadIdx.x; e < W; e += (int)blockDim.x) nsq = nsq + buf[e] * buf[e];
         const T nn = sqrt(block_sum(nsq, red));
         const T sn_ = pmax(nn, eps);
         int fin = 1;
         T* Vn = V + (size_t)(it + 1) * W;
-        for (int e = threadIdx.x; e < W; e += kThreads) {
+        for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
           const T v = buf[e] / sn_;
           buf[e] = v;
           Vn[e] = v;
@@ -587,7 +596,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       }
       __syncthreads();
 #pragma unroll 2
-      for (int e = threadIdx.x; e < W; e += kThreads) {
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
         const T cand = x[e] + basis_combination(V, W, e, row_steps, bsv);
         buf[e] = cand;
         x[e] = cand;
@@ -595,7 +604,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       __syncthreads();
       apply_operator(st, s, buf, tn, tm);
       T cn = zero;
-      for (int e = threadIdx.x; e < W; e += kThreads) cn = pmax(cn, fabs(rhs_entry(s, n, m, e) - buf[e]));
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) cn = pmax(cn, fabs(rhs_entry(s, n, m, e) - buf[e]));
       cn = block_max(cn, red);
       if (threadIdx.x == 0) {
         p.resinf[X] = cn;
@@ -618,17 +627,17 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
   for (int64_t X = blockIdx.x; (stage == 0 || stage == 3) && X < p.batch; X += gridDim.x) {
     if (p.converged[X] == 0) {
       // Zero right-hand side: zero solution (status 0, residual 0), zero gradients.
-      for (int j = threadIdx.x; j < n; j += kThreads) {
+      for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
         if (p.g_target) p.g_target[X * n + j] = zero;
         if (p.g_lower) p.g_lower[X * n + j] = zero;
         if (p.g_upper) p.g_upper[X * n + j] = zero;
         if (p.g_q) p.g_q[X * n + j] = zero;
         if (p.g_c) p.g_c[X * n + j] = zero;
       }
-      for (int i = threadIdx.x; i < m; i += kThreads)
+      for (int i = threadIdx.x; i < m; i += (int)blockDim.x)
         if (p.g_rhs) p.g_rhs[X * m + i] = zero;
       if (p.g_values)
-        for (int k = threadIdx.x; k < st.nnz; k += kThreads) p.g_values[X * st.nnz + k] = zero;
+        for (int k = threadIdx.x; k < st.nnz; k += (int)blockDim.x) p.g_values[X * st.nnz + k] = zero;
       if (threadIdx.x == 0) {
         if (p.lin_status) p.lin_status[X] = 0;
         if (p.lin_residual) p.lin_residual[X] = zero;
@@ -638,7 +647,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     const Sample<T> s = make_sample(p, X);
     const T* x = p.x + X * W;
     int fin = 1;
-    for (int e = threadIdx.x; e < W; e += kThreads) {
+    for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
       const T v = x[e];
       buf[e] = v;
       fin &= finite(v) ? 1 : 0;
@@ -650,13 +659,13 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     const int code = !fin_all ? 2 : (ri <= thr ? 0 : 1);
     const bool valid = s.conv && fin && finite(ri) && (code == 0 || ri <= p.adj_tol);
     if (!valid) {
-      for (int e = threadIdx.x; e < W; e += kThreads) buf[e] = zero;
+      for (int e = threadIdx.x; e < W; e += (int)blockDim.x) buf[e] = zero;
     }
     __syncthreads();
     const T* zy = buf;
     const T* zd = buf + n;
     const T* zb = buf + n + m;
-    for (int j = threadIdx.x; j < n; j += kThreads) {
+    for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
       const T vy = zy[j], vb = zb[j];
       const T gg = (vy + vb) + vb;
       const int code_j = s.yc[j];
@@ -685,7 +694,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       if (p.g_upper) p.g_upper[X * n + j] = clean(gup);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < m; i += kThreads) {
+    for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
       T acc = zero;
       for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * tn[st.col[k]];
       const T mu = zd[i] + acc;
@@ -717,6 +726,15 @@ size_t small_elems(int R) {
 
 }  // namespace
 
+int adjoint_threads(int n, int m) {
+  if (const char* env = std::getenv("PURIN_CP_ADJOINT_THREADS")) {
+    const int t = std::atoi(env);
+    if (t == kSmallThreads || t == kThreads) return t;
+  }
+  return 2 * (int64_t)n + m <= (int64_t)kSmallEntriesPerThread * kSmallThreads ? kSmallThreads
+                                                                               : kThreads;
+}
+
 template <typename T>
 size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors) {
   const size_t W = 2 * (size_t)n + m;
@@ -728,18 +746,19 @@ size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors) {
 template <typename T>
 int adjoint_grid(int sm_count, int n, int m, int R, bool smem_vectors, int64_t batch) {
   const size_t smem = adjoint_smem_bytes<T>(n, m, R, smem_vectors);
+  const int threads = adjoint_threads(n, m);
   int per_sm = 0;
   if (smem_vectors) {
     auto kern = cp_adjoint_kernel<T, true>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
       return 0;
   } else {
     auto kern = cp_adjoint_kernel<T, false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
       return 0;
   }
   int64_t grid = (int64_t)per_sm * sm_count;
@@ -755,10 +774,11 @@ cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors, c
   auto kern = smem_vectors ? cp_adjoint_kernel<T, true> : cp_adjoint_kernel<T, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  const int threads = adjoint_threads(n, m);
   // Only the fused launch has grid barriers, so only it needs co-residency.
   if (p.stage == 0)
-    return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
-  return cudaLaunchKernel((void*)kern, dim3(grid), dim3(kThreads), args, smem, stream);
+    return cudaLaunchCooperativeKernel((void*)kern, dim3(grid), dim3(threads), args, smem, stream);
+  return cudaLaunchKernel((void*)kern, dim3(grid), dim3(threads), args, smem, stream);
 }
 
 template size_t adjoint_smem_bytes<double>(int, int, int, bool);
