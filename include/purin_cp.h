@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define PURIN_CP_ABI_VERSION 1
+#define PURIN_CP_ABI_VERSION 2  /* 2: PurinQpForwardArgs gained flags and the resume fields */
 
 typedef enum PurinStatus {
   PURIN_OK = 0,
@@ -329,6 +329,17 @@ typedef struct PurinQpForwardArgs {
   uint8_t* converged;       /* out (B,)                                      */
   int32_t flags;            /* 0 for PreparedDiagonalQP; PURIN_QP_* bits for
                                the dense adapter's variant of sparse_cp     */
+  /* Resuming a solve (NULL = start afresh).  With y0, dual0, ybar0 and
+   * start_iterations taken from an earlier call's y, dual, ybar and
+   * iterations, each sample continues exactly as if that call had kept
+   * iterating: the accelerated step sizes are advanced start_iterations[b]
+   * times, the loop runs from start_iterations[b] to max_iterations, and
+   * iterations[b] counts from there.  residual, gap and converged then cover
+   * only the iterations run in this call (0, 0 and 0 for a sample with none).
+   * The dense adapter's batch-wide trip count uses this (dense.py:79-99). */
+  const void* ybar0;                /* in (B, n) or NULL (ybar = y0)         */
+  const int32_t* start_iterations;  /* in (B,) or NULL (0); needs y0         */
+  void* ybar;                       /* out (B, n) or NULL: final ybar        */
 } PurinQpForwardArgs;
 
 /* purin_qp_forward flags: the sparse_cp options the dense adapter

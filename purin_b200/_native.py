@@ -13,7 +13,7 @@ from pathlib import Path
 import numpy as np
 
 _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpurin_cp.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 PURIN_FLOAT64, PURIN_FLOAT32 = 0, 1
 OP_FORWARD, OP_ADJOINT, QP_OP_FORWARD, QP_OP_ADJOINT = 0, 1, 2, 3
@@ -72,7 +72,7 @@ class QpForwardArgs(ctypes.Structure):
                 ("bounds_stride", c_i64), ("y0", c_vp), ("dual0", c_vp), ("tolerance", c_vp),
                 ("sample_offset", c_i64), ("total_batch", c_i64), ("y", c_vp), ("dual", c_vp),
                 ("iterations", c_vp), ("residual", c_vp), ("gap", c_vp), ("converged", c_vp),
-                ("flags", c_i32)]
+                ("flags", c_i32), ("ybar0", c_vp), ("start_iterations", c_vp), ("ybar", c_vp)]
 
 
 QP_FACTORED_PROXIMAL, QP_NO_STATIONARITY, QP_NO_FREEZE, QP_NO_VALIDITY = 1, 2, 4, 8

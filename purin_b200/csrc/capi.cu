@@ -62,6 +62,7 @@ struct FwdPlan {
   size_t off_vr = 0, off_vc = 0, off_state = 0;
   size_t off_tgt = 0, off_rhs = 0, off_dual0 = 0, off_lo = 0, off_up = 0;
   size_t off_q = 0, off_c = 0, off_y0 = 0;  // diagonal QP inputs (internal order)
+  size_t off_ybar0 = 0;                     // resumed QP solve: ybar (internal order)
   size_t off_vr_ps = 0, off_vc_ps = 0;      // per-sample values in the SELL orders
   size_t off_dg = 0;                        // shared diagonal steps (sigma, tau, a, d)
   int sell_index = 0;  // log2(32 / C), C = 32 / S
@@ -94,8 +95,9 @@ FwdPlan plan_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   fp.off_q = fp.off_up + align_up(nb * sv.n_pos * w);
   fp.off_c = fp.off_q + qp_vec;
   fp.off_y0 = fp.off_c + qp_vec;
+  fp.off_ybar0 = fp.off_y0 + qp_vec;
   const size_t ps = shared_values ? 0 : nb;
-  fp.off_vr_ps = fp.off_y0 + qp_vec;
+  fp.off_vr_ps = fp.off_ybar0 + qp_vec;
   fp.off_vc_ps = fp.off_vr_ps + align_up(ps * sv.nnz_r * w);
   // Diagonal steps of shared values: once per call, m_pos + 3 n_pos scalars.
   const bool dg = cfg->diagonal_preconditioning && !cfg->accelerated && shared_values;
@@ -273,6 +275,9 @@ struct QpInputs {
   const void* c;
   const void* y0;
   int32_t flags;
+  const void* ybar0;               // resume: extrapolated iterate (null: y0)
+  const int32_t* start_iterations;  // resume: iterations already run (null: 0)
+  void* ybar;                       // out: final extrapolated iterate (null: not written)
 };
 
 template <typename T>
@@ -323,6 +328,7 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   T* q_i = qp ? reinterpret_cast<T*>(ws + fp.off_q) : nullptr;
   T* c_i = qp ? reinterpret_cast<T*>(ws + fp.off_c) : nullptr;
   T* y0_i = (qp && qp->y0) ? reinterpret_cast<T*>(ws + fp.off_y0) : nullptr;
+  T* ybar0_i = (qp && qp->ybar0) ? reinterpret_cast<T*>(ws + fp.off_ybar0) : nullptr;
   {
     const int n = plan->info.n, m = plan->info.kept_rows;
     cudaError_t e = cudaSuccess;
@@ -334,6 +340,9 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
       if (e == cudaSuccess && y0_i)
         e = purin::permute_rows<T>(static_cast<const T*>(qp->y0), n, sv.c_perm, sv.n_pos, a->batch, y0_i,
                                    stream);
+      if (e == cudaSuccess && ybar0_i)
+        e = purin::permute_rows<T>(static_cast<const T*>(qp->ybar0), n, sv.c_perm, sv.n_pos, a->batch,
+                                   ybar0_i, stream);
     } else {
       e = purin::permute_rows<T>(static_cast<const T*>(a->target), n, sv.c_perm, sv.n_pos, a->batch, tgt_i,
                                  stream);
@@ -360,6 +369,9 @@ int32_t run_forward(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   p.c_i = c_i;
   p.y0_i = y0_i;
   p.qp_flags = qp ? qp->flags : 0;
+  p.ybar0_i = ybar0_i;
+  p.start_it = qp ? qp->start_iterations : nullptr;
+  p.ybar_out = qp ? static_cast<T*>(qp->ybar) : nullptr;
   p.rhs_i = rhs_i;
   p.dual0_i = (dual0_i && plan->info.kept_rows > 0) ? dual0_i : nullptr;
   p.lo_i = lo_i;
@@ -1195,7 +1207,12 @@ int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, c
   if (args->flags & ~(PURIN_QP_FACTORED_PROXIMAL | PURIN_QP_NO_STATIONARITY | PURIN_QP_NO_FREEZE |
                       PURIN_QP_NO_VALIDITY))
     return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown purin_qp_forward flags");
-  const QpInputs qp{args->q, args->c, args->y0, args->flags};
+  if ((args->ybar0 || args->start_iterations) && !args->y0)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "resuming a QP solve (ybar0, start_iterations) needs y0");
+  const QpInputs qp{args->q,     args->c,
+                    args->y0,    args->flags,
+                    args->ybar0, args->start_iterations,
+                    args->ybar};
   DeviceGuard guard(plan->info.device);
   if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

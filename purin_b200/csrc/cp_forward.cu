@@ -454,6 +454,23 @@ cp_forward_kernel(const FwdParams<T> p) {
     }
   }
 
+  // Accelerated step-size update after an iteration (kernels.py:289-297).
+  auto advance_steps = [&](int q) {
+    const T tau = sc.tau[q];
+    const T nt = one / sqrt(one + sc.gam[q] * tau);
+    const T ntau = nt * tau;
+    sc.tau[q] = ntau;
+    sc.sigma[q] = sc.sigma[q] / nt;
+    sc.theta[q] = nt;
+    sc.a[q] = one / (one + ntau * one);
+    sc.d[q] = ntau * sc.a[q];
+  };
+  // Iterations a resumed sample has already run, within [0, max_iterations].
+  auto resume_iteration = [&](int q) {
+    const int v = p.start_it[sample(q)];
+    return v < 0 ? 0 : (v > p.max_iterations ? p.max_iterations : v);
+  };
+
   // ---- initial state: y = ybar = y0 (the target), lambda = dual0 -----------
   for (int pp = tid; pp < n_pos; pp += kThreads) {
     T t[S];
@@ -463,6 +480,12 @@ cp_forward_kernel(const FwdParams<T> p) {
       else t[q] = p.tgt_i[sample(q) * n_pos + pp];
     }
     store_pack<T, S>(y + (size_t)pp * S, t);
+    if constexpr (kQP) {
+      if (p.ybar0_i) {
+#pragma unroll
+        for (int q = 0; q < S; ++q) t[q] = p.ybar0_i[sample(q) * n_pos + pp];
+      }
+    }
     store_pack<T, S>(ybar + (size_t)pp * S, t);
   }
   for (int qp = tid; qp < m_pos; qp += kThreads) {
@@ -487,6 +510,16 @@ cp_forward_kernel(const FwdParams<T> p) {
     sc.tol[q] = p.tol[sample(q)];
     sc.active[q] = is_valid(q) ? 1 : 0;
     sc.count[q] = 0;
+    if constexpr (kQP) {
+      // Resuming after start_it iterations: the count and the accelerated
+      // steps continue from there (the same updates the loop applies).
+      if (p.start_it && is_valid(q)) {
+        const int it0 = resume_iteration(q);
+        sc.count[q] = it0;
+        if (p.accelerated)
+          for (int k = 0; k < it0; ++k) advance_steps(q);
+      }
+    }
     sc.conv[q] = 0;
     sc.res_out[q] = zero;
     sc.gap_out[q] = zero;
@@ -631,7 +664,11 @@ cp_forward_kernel(const FwdParams<T> p) {
   // phases A and B (a converging tile needs it on most later iterations); before
   // that, phase B2 recomputes the same sums in the same order when required.
   bool full = false;
-  for (int it = 0; it < p.max_iterations; ++it) {
+  int it_begin = 0;
+  if constexpr (kQP && S == 1) {
+    if (p.start_it && is_valid(0)) it_begin = resume_iteration(0);
+  }
+  for (int it = it_begin; it < p.max_iterations; ++it) {
     int act = 0;
 #pragma unroll
     for (int q = 0; q < S; ++q) act |= (sc.active[q] != 0) << q;
@@ -816,16 +853,7 @@ cp_forward_kernel(const FwdParams<T> p) {
         // runs the batch's trip count; kernels.py:266-271).
         if (accepted && !(kQP && (p.qp_flags & 4))) sc.active[q] = 0;
       }
-      if (p.accelerated) {
-        const T tau = sc.tau[q];
-        const T nt = one / sqrt(one + sc.gam[q] * tau);
-        const T ntau = nt * tau;
-        sc.tau[q] = ntau;
-        sc.sigma[q] = sc.sigma[q] / nt;
-        sc.theta[q] = nt;
-        sc.a[q] = one / (one + ntau * one);
-        sc.d[q] = ntau * sc.a[q];
-      }
+      if (p.accelerated) advance_steps(q);
     }
     __syncthreads();
   }
@@ -838,6 +866,13 @@ cp_forward_kernel(const FwdParams<T> p) {
     for (int pp = tid; pp < n_pos; pp += kThreads) {
       const int j = __ldg(sv.c_perm + pp);
       if (j >= 0) p.y_out[b * n + j] = y[(size_t)pp * S + q];
+    }
+    if constexpr (kQP) {
+      if (p.ybar_out)
+        for (int pp = tid; pp < n_pos; pp += kThreads) {
+          const int j = __ldg(sv.c_perm + pp);
+          if (j >= 0) p.ybar_out[b * n + j] = ybar[(size_t)pp * S + q];
+        }
     }
     for (int qp = tid; qp < m_pos; qp += kThreads) {
       const int i = __ldg(sv.r_perm + qp);

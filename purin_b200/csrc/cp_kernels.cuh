@@ -75,6 +75,14 @@ struct FwdParams {
   // the projection and the diagonal QP): PURIN_QP_FACTORED_PROXIMAL,
   // PURIN_QP_NO_STATIONARITY, PURIN_QP_NO_FREEZE, PURIN_QP_NO_VALIDITY bits.
   int qp_flags;
+  // Resuming a solve (kQP kernels, one-sample tiles): the extrapolated iterate
+  // in the internal column order (null: ybar = y0), the iterations each sample
+  // has already run (null: 0; the accelerated step sizes are advanced that many
+  // times and the count starts there), and the final extrapolated iterate in
+  // the external order (null: not written).
+  const T* ybar0_i;
+  const int32_t* start_it;
+  T* ybar_out;
 };
 
 template <typename T>

@@ -16,7 +16,8 @@ implicitly.  It runs on the diagonal-QP kernels (``purin_qp_forward`` /
   iteration at which the last sample is first accepted.  A first pass with
   freezing finds that count (a sample's iterates up to its first acceptance do
   not depend on freezing); when samples differ, a second pass without freezing
-  runs every sample exactly that many iterations;
+  resumes each sample from its first-pass state and runs it on to that count,
+  so the kernels execute the batch's trip count per sample and no more;
 * equality rows dense; inequality rows dense, or packed on
   ``inequality_support``.
 
@@ -156,11 +157,13 @@ class _DenseSolver:
     def stream(self):
         return ctypes_stream(torch.cuda.current_stream(self.device))
 
-    def forward(self, inputs, max_iterations, flags):
+    def forward(self, inputs, max_iterations, flags, *, ybar0=None, start=None):
+        """One ``purin_qp_forward`` call; ``ybar0`` and ``start`` resume an earlier one."""
         q, c, values, rhs, lower, upper, y0, dual0, tolerance = inputs
         batch, n = q.shape
         dev, dt = q.device, q.dtype
         out = dict(y=torch.empty((batch, n), dtype=dt, device=dev),
+                   ybar=torch.empty((batch, n), dtype=dt, device=dev),
                    dual=torch.empty((batch, self.m), dtype=dt, device=dev),
                    iterations=torch.empty((batch,), dtype=torch.int32, device=dev),
                    residual=torch.empty((batch,), dtype=dt, device=dev),
@@ -175,7 +178,8 @@ class _DenseSolver:
             batch, _ptr(q), _ptr(c), _ptr(values), 0 if shared else values.shape[1], _ptr(rhs),
             _ptr(lower), _ptr(upper), n, _ptr(y0), _ptr(dual0), _ptr(tolerance), 0, batch,
             _ptr(out["y"]), _ptr(out["dual"]), _ptr(out["iterations"]), _ptr(out["residual"]),
-            _ptr(out["gap"]), _ptr(out["converged"]), int(flags))
+            _ptr(out["gap"]), _ptr(out["converged"]), int(flags), _ptr(ybar0), _ptr(start),
+            _ptr(out["ybar"]))
         with _timed("forward", self.device):
             self.plan.qp_forward(cfg, args, ws.data_ptr(), ws_bytes, self.stream())
         return out
@@ -194,9 +198,13 @@ class _DenseSolve(torch.autograd.Function):
         solver.last_work = [int(iterations.sum().item())]
         if bool((iterations != trips).any()):
             # Samples accepted before the last one keep iterating in the
-            # reference's shared loop: rerun every sample the batch's trip count.
-            out = solver.forward(inputs, trips, _FIRST_PASS | _native.QP_NO_FREEZE)
-            solver.last_work.append(trips * iterations.numel())
+            # reference's shared loop: each resumes from its state at its own
+            # first acceptance (y, dual, ybar, iteration count) and runs on to
+            # the batch's trip count.
+            resumed = (q, c, values, rhs, lower, upper, out["y"], out["dual"], tolerance)
+            out = solver.forward(resumed, trips, _FIRST_PASS | _native.QP_NO_FREEZE,
+                                 ybar0=out["ybar"], start=iterations)
+            solver.last_work.append(trips * iterations.numel() - solver.last_work[0])
         ctx.solver = solver
         ctx.save_for_backward(q, c, values, rhs, lower, upper, out["y"], out["dual"])
         ctx.mark_non_differentiable(out["iterations"])

@@ -209,3 +209,41 @@ def test_dense_edge_cases_match_oracle(case):
         np.testing.assert_allclose(g.cpu().numpy(), r, rtol=1e-9, atol=1e-11)
     if case == "max_iterations_reached":
         assert ref[3].tolist() == [180] * 4
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+def test_qp_forward_resume_is_bitwise_uninterrupted(accelerated):
+    """purin_qp_forward resumed from (y, dual, ybar, iterations) = one uninterrupted run.
+
+    Pass 1 freezes each sample at its first acceptance; pass 2 resumes every
+    sample from there without freezing.  The result must equal, bit for bit,
+    a single run without freezing for the same trip count.
+    """
+    from purin_b200 import _native
+    from purin_b200.config import ChambollePockConfig, LinearSolverConfig
+    from purin_b200.dense_layer import _FIRST_PASS, _DenseSolver
+    from purin_b200.layer import resolve_device
+
+    q, c, A, b, C, d, lo, hi = (torch.as_tensor(x, device=DEV)
+                                for x in _random_dense(4, 6, 2, 3, seed=3))
+    n, me, mi = 6, 2, 3
+    cfg = ChambollePockConfig(accelerated=accelerated, tolerance=1e-8, max_iterations=4000,
+                              norm_bound=False, row_scaling=False,
+                              linear_solver=LinearSolverConfig())
+    solver = _DenseSolver(n, me, tuple(tuple(range(n)) for _ in range(mi)), torch.float64,
+                          resolve_device(DEV), cfg)
+    values = torch.cat((A.reshape(4, -1), C.reshape(4, -1)), dim=1).contiguous()
+    rhs = torch.cat((b, d), dim=1).contiguous()
+    zeros = lambda k: torch.zeros((4, k), dtype=torch.float64, device=DEV)
+    tol = torch.full((4,), 1e-8, dtype=torch.float64, device=DEV)
+    inputs = (q, c, values, rhs, lo, hi, zeros(n), zeros(me + mi), tol)
+    first = solver.forward(inputs, 4000, _FIRST_PASS)
+    trips = int(first["iterations"].max())
+    assert len(set(first["iterations"].tolist())) > 1 and trips < 4000
+    resumed_inputs = (q, c, values, rhs, lo, hi, first["y"], first["dual"], tol)
+    resumed = solver.forward(resumed_inputs, trips, _FIRST_PASS | _native.QP_NO_FREEZE,
+                             ybar0=first["ybar"], start=first["iterations"])
+    whole = solver.forward(inputs, trips, _FIRST_PASS | _native.QP_NO_FREEZE)
+    for key in ("y", "ybar", "dual"):
+        assert torch.equal(resumed[key], whole[key]), key
+    assert resumed["iterations"].tolist() == [trips] * 4 == whole["iterations"].tolist()
