@@ -45,9 +45,10 @@ namespace {
 // it); every loop and reduction uses blockDim.x, so a launch may use fewer.
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-// Krylov vectors of at most this many entries per thread run on kSmallThreads:
-// a small sample gets half the threads and an SM twice the samples in flight
-// at the same register budget (the per-sample phases are barrier-bound).
+// Krylov vectors of at most this many entries per thread run on kSmallThreads
+// (or half of it): a small sample gets a half or a quarter of the threads and
+// an SM two or four times the samples in flight at the same register budget
+// (the per-sample phases are barrier-bound).
 constexpr int kSmallThreads = 128;
 constexpr int kSmallEntriesPerThread = 4;
 constexpr int kChunk = 8;  // basis vectors per register-resident dot-product chunk
@@ -729,10 +730,11 @@ size_t small_elems(int R) {
 int adjoint_threads(int n, int m) {
   if (const char* env = std::getenv("PURIN_CP_ADJOINT_THREADS")) {
     const int t = std::atoi(env);
-    if (t == kSmallThreads || t == kThreads) return t;
+    if (t == kSmallThreads / 2 || t == kSmallThreads || t == kThreads) return t;
   }
-  return 2 * (int64_t)n + m <= (int64_t)kSmallEntriesPerThread * kSmallThreads ? kSmallThreads
-                                                                               : kThreads;
+  const int64_t W = 2 * (int64_t)n + m;
+  if (W <= (int64_t)kSmallEntriesPerThread * (kSmallThreads / 2)) return kSmallThreads / 2;
+  return W <= (int64_t)kSmallEntriesPerThread * kSmallThreads ? kSmallThreads : kThreads;
 }
 
 template <typename T>
