@@ -2,8 +2,12 @@
 
 Contract: ``python bench.py --gpus N --steps K --warmup W [--impl reference]`` prints
 ONE JSON line.  For N > 1 it runs under ``torch.distributed.run`` with one rank
-per GPU; every rank solves its own shard of samples (weak scaling, no data-path
-collective) and the step time is the maximum over ranks.
+per GPU; the ranks share one seeded global batch of N x B samples and rank r
+solves samples [r B, (r + 1) B) (weak scaling; the forward needs no exchange,
+the adjoint's GMRES counters are all-reduced once per cycle so the shards share
+the batch's budget) and the step time is the maximum over ranks.  The line
+carries a checksum of every rank's projections (``shard_checksums``), which a
+1-GPU run over the same global batch reproduces slice by slice.
 
 Workload: benchmark configuration 2 (fp64, B = 2048 per GPU, n = 2048,
 me = 512, mi = 1024, 8 nnz per row, box bounds as 2n singleton rows, fixed
@@ -164,6 +168,19 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def shard_checksums(y, world, device):
+    """Sum of each rank's projections (fp64), gathered on every rank in rank order."""
+    import torch
+    import torch.distributed as dist
+
+    local = y.detach().double().sum().reshape(1)
+    if world == 1:
+        return [float(local.item())]
+    parts = [torch.zeros_like(local) for _ in range(world)]
+    dist.all_gather(parts, local)
+    return [float(p.item()) for p in parts]
+
+
 def count_native_launches(step, device):
     """Kernels of this library (namespace purin) launched by one untimed step, from the profiler."""
     import torch
@@ -291,7 +308,8 @@ def main_qp(args, world, rank, local_rank, device, barrier):
 
     batch = args.batch or DEFAULT_BATCH[CONFIG_INDEX]
     total = batch * world
-    structure, q, c, values, rhs, lower, upper, targets = qp_workload(batch, seed=rank)
+    # Every rank holds the same structure and its own slice of one global batch.
+    structure, q, c, values, rhs, lower, upper, targets = qp_workload(batch, offset=rank * batch)
     cfg = ChambollePockConfig(max_iterations=2000)
     if args.cp_tolerance is not None:
         cfg = dataclasses.replace(cfg, tolerance=args.cp_tolerance)
@@ -467,7 +485,7 @@ def main_dense(args, world, rank, local_rank, device, barrier):
 
     batch = args.batch or 16384
     total = batch * world
-    problem = dense_workload(batch, seed=rank)
+    problem = dense_workload(batch, offset=rank * batch)  # this rank's slice of the batch
     q, c, A, b, C, d, lower, upper, targets = problem
     n, me, mi = q.shape[1], A.shape[1], C.shape[1]
     m = me + mi
@@ -638,7 +656,11 @@ def main():
     vjp = (args.mode or ("fwd+vjp" if index == CONFIG_INDEX else "fwd")) == "fwd+vjp"
     batch = args.batch or DEFAULT_BATCH[index]
     total = batch * world
-    workload = make_workload(index, batch, seed=rank, dtype=args.dtype)
+    # Every rank builds the same seed-0 structure and takes its slice
+    # [rank * batch, (rank + 1) * batch) of one global batch of world * batch samples.
+    fp32 = (args.dtype or ("float32" if index in (3, 4) else "float64")) == "float32"
+    workload = make_workload(index, batch, dtype=args.dtype, offset=rank * batch,
+                             array_dtype=np.float32 if fp32 else np.float64)
     tdt = torch.float64 if workload.dtype == "float64" else torch.float32
     cfg = workload.config
     if workload.weights is not None:  # configuration 4: WeightedDistance
@@ -658,8 +680,7 @@ def main():
 
     cand_d = torch.as_tensor(workload.candidates, dtype=tdt, device=device)
     theta_d = torch.as_tensor(workload.theta, dtype=tdt, device=device)
-    targets = (workload.targets if workload.targets is not None
-               else np.random.default_rng(1000 + rank).normal(size=(batch, n)))
+    targets = workload.targets
     targ_d = torch.as_tensor(targets, dtype=tdt, device=device)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
@@ -712,6 +733,7 @@ def main():
     with torch.no_grad():
         result = layer.solve(cand_d, theta_d)
     iters_total = int(result.iterations.sum().item())
+    checksums = shard_checksums(result.y, world, device)
     # Per step: the staged adjoint of a multi-rank run records one entry per phase.
     per_step = lambda name: (sum(per_kernel[name]) / args.steps if name in per_kernel
                              else float("nan"))
@@ -817,6 +839,7 @@ def main():
                         "traffic, not this kernel's",
             },
             "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms, "postprocess": post_ms},
+            "shard_checksums": checksums,
             "gpu_launches": launches,
             "e2e": {"value": total / (e2e / 1000.0), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e},

@@ -409,10 +409,15 @@ int32_t purin_qp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* con
  * (one copy on every GPU that loads the library, kept until the process
  * exits).  The call allocates nothing; inputs and outputs are the caller's, as
  * for purin_cp_forward, and results are identical.  Problems whose scratch
- * (purin_cp_workspace_size with PURIN_CP_OP_FORWARD) exceeds the array are
- * rejected with PURIN_ERR_WORKSPACE.  The first call on a device looks up the
- * array's device address with that device current; make that first call
- * before any stream capture.  All calls on a device share the one array, so
+ * exceeds the array are rejected with PURIN_ERR_WORKSPACE: the scratch is
+ * purin_cp_workspace_size with PURIN_CP_OP_FORWARD for values shared by the
+ * batch (values_stride 0, or batch 1), and with
+ * PURIN_CP_OP_FORWARD_SAMPLE_VALUES for values given per sample, which also
+ * hold every sample's values in the kernels' two sparse orders.  The call sets
+ * the plan's device current for its duration and restores the caller's.  The
+ * first call on a device looks up the array's device address with that device
+ * current; make that first call before any stream capture.  All calls on a
+ * device share the one array, so
  * calls whose executions overlap on the GPU (other streams, other host
  * threads) race: serialise them. */
 #define PURIN_CP_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)

@@ -1294,6 +1294,11 @@ extern "C" int32_t purin_cp_forward_noalloc(const PurinCpPlan* plan, const Purin
   const int device = plan->info.device;
   if (device < 0 || device >= kNoAllocMaxDevices)
     return fail(PURIN_ERR_UNSUPPORTED, "purin_cp_forward_noalloc supports device ordinals below 128");
+  // The tile planner queries kernel attributes and occupancy, and the symbol
+  // lookup below resolves the array, on the CURRENT device: make it the plan's
+  // before either, so no other GPU gets a context (and a copy of the array).
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
   const bool shared = args->values_stride == 0 || args->batch == 1 || plan->info.kept_nnz == 0;
   const size_t need = plan_forward(plan, config, args->batch, shared).workspace;
   if (need > kNoAllocScratchBytes)
@@ -1307,8 +1312,6 @@ extern "C" int32_t purin_cp_forward_noalloc(const PurinCpPlan* plan, const Purin
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     scratch = g_noalloc_address[device];
     if (scratch == nullptr) {
-      DeviceGuard guard(device);
-      if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
       cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
       if (e != cudaSuccess) return cuda_fail(e, "purin_cp_forward_noalloc cudaGetSymbolAddress");
       g_noalloc_address[device] = scratch;

@@ -46,8 +46,8 @@ def test_config0_matches_numpy_loop(overrides):
 
 def test_ragged_rows_match_numpy_loop():
     """Network-flow rows of different lengths: padded slots in the row layout."""
-    problem, theta, candidates = network_flow_config(batch=4, nodes=60, edges=200, couplings=40,
-                                                     seed=3)
+    problem, theta, candidates, _ = network_flow_config(batch=4, nodes=60, edges=200,
+                                                        couplings=40, seed=3)
     _compare(problem, ChambollePockConfig(max_iterations=300), candidates, theta)
 
 
