@@ -84,6 +84,9 @@ def parse_args():
     p.add_argument("--cpu-samples", type=int, default=None,
                    help="samples in the CPU baseline (default 48 per host core, ~15 s)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--vjp-active-tolerance", type=float, default=1e-3,
+                   help="CP tolerance of the extra GMRES-active VJP measurement that the "
+                        "configuration-2 fwd+VJP line carries as 'vjp_active' (0 to skip)")
     p.add_argument("--cp-tolerance", type=float, default=None,
                    help="override the CP stopping tolerance (default: the workload's 1e-9); "
                         "a loose value such as 1e-3 lets samples converge so that the VJP "
@@ -179,6 +182,105 @@ def shard_checksums(y, world, device):
     parts = [torch.zeros_like(local) for _ in range(world)]
     dist.all_gather(parts, local)
     return [float(p.item()) for p in parts]
+
+
+def measure_vjp_active(args, workload, cfg, batch, world, device, barrier, tdt):
+    """The headline step with the CP tolerance loosened so samples are accepted and the
+    implicit VJP runs its restarted GMRES (the reference's LinearSolverConfig defaults).
+
+    At the headline's tolerance 1e-9 no sample is accepted within 2000 iterations, so
+    the reference gates every gradient to zero without solving (bounds.py:133) and the
+    adjoint kernel does almost no work.  This measurement times the same step where it
+    does: samples/s, the forward and adjoint kernel times, the Arnoldi steps GMRES took
+    (the kernel's own counters) and the adjoint's algorithmic HBM bytes
+    sum_steps (4k + 6) W w + 20 (2n + m) w per linearised sample (k basis vectors at a
+    step; W = 2n + m) against the measured copy peak.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from purin_b200 import prepare_projection
+
+    cfg = dataclasses.replace(cfg, tolerance=args.vjp_active_tolerance)
+    layer = prepare_projection(workload.problem, method="chambolle-pock", config=cfg,
+                               batch_size=batch, dtype=tdt, backend=str(device))
+    layer.set_shard(int(os.environ.get("RANK", "0")) * batch, batch * world,
+                    group=dist.group.WORLD if world > 1 else None)
+    cand = torch.as_tensor(workload.candidates, dtype=tdt, device=device)
+    theta = torch.as_tensor(workload.theta, dtype=tdt, device=device)
+    targ = torch.as_tensor(workload.targets, dtype=tdt, device=device)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def step():
+        x = cand.detach().requires_grad_(True)
+        th = theta.detach().requires_grad_(True)
+        y = layer(x, th)
+        (0.5 * ((y - targ) ** 2).sum()).backward()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    timers, step_ms = [], []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        layer.record_launches(timers)
+        start.record()
+        step()
+        end.record()
+        layer.record_launches(None)
+        torch.cuda.synchronize(device)
+        step_ms.append(start.elapsed_time(end))
+    barrier()
+    per_kernel = {}
+    for name, s0, e0 in timers:
+        per_kernel.setdefault(name, []).append(s0.elapsed_time(e0))
+    fwd_ms = sum(per_kernel.get("forward", [0.0])) / args.steps
+    adj_ms = sum(per_kernel.get("adjoint", [0.0])) / args.steps
+    steps, vectors = layer._last_work
+    status, _ = layer._last_linear
+    with torch.no_grad():
+        result = layer.solve(cand, theta)
+    n = workload.problem.variable_size
+    m = layer._m
+    w = 8 if tdt == torch.float64 else 4
+    W = 2 * n + m
+    linearised = int(result.gradient_eligible.sum().item())
+    local = torch.tensor([float(sum(step_ms) / len(step_ms)), fwd_ms, adj_ms], device=device,
+                         dtype=torch.float64)
+    totals = torch.tensor([float(steps.sum().item()), float(vectors.sum().item()),
+                           float(linearised), float(result.iterations.sum().item())],
+                          device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(local, op=dist.ReduceOp.MAX)
+        dist.all_reduce(totals, op=dist.ReduceOp.SUM)
+    ms, fwd_ms, adj_ms = (float(v) for v in local.tolist())
+    arnoldi, krylov, linearised_all, iters_all = (float(v) for v in totals.tolist())
+    # Per rank, the adjoint launch processes its own shard: bytes per launch are the
+    # job's bytes divided by the ranks (one launch per rank and step).
+    vjp_bytes = ((4.0 * krylov + 6.0 * arnoldi) * W * w
+                 + 20.0 * (2 * n + m) * w * linearised_all) / world
+    fwd_bytes = algorithmic_bytes_forward(n, m, w, iters_all) / world
+    hbm, peak_kind = peaks()
+    adj_gbs = vjp_bytes / (adj_ms / 1000.0) / 1e9 if adj_ms > 0 else None
+    return {
+        "cp_tolerance": args.vjp_active_tolerance,
+        "value": batch * world / (ms / 1000.0), "unit": "samples/s", "ms_per_step": ms,
+        "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms},
+        "gradient_eligible": f"{int(linearised_all)}/{batch * world}",
+        "gmres_codes_rank0": {str(c): int((status == c).sum().item()) for c in (0, 1, 2)},
+        "arnoldi_steps": int(arnoldi), "krylov_vectors": int(krylov),
+        "adjoint_roofline": {
+            "bound": "hbm", "kernel": "cp_adjoint_kernel", "achieved": adj_gbs, "peak": hbm,
+            "unit": "GB/s", "frac": adj_gbs / hbm if adj_gbs else None,
+            "peak_source": peak_kind, "algorithmic_bytes_per_launch": vjp_bytes,
+            "launch_ms": adj_ms,
+            "note": "sum over Arnoldi steps of (4k+6)*W*w (CGS2 with k basis vectors) + "
+                    "20*(2n+m)*w power iteration per linearised sample",
+        },
+        "forward_algorithmic_gbs": fwd_bytes / (fwd_ms / 1000.0) / 1e9 if fwd_ms > 0 else None,
+    }
 
 
 def count_native_launches(step, device):
@@ -799,8 +901,11 @@ def main():
         h2d = (cand_h.numel() + theta_h.numel()) * w
         d2h = gx_h.numel() * w
 
-    cpu = None
     headline = index == CONFIG_INDEX and vjp and tdt == torch.float64
+    vjp_active = None
+    if headline and args.vjp_active_tolerance > 0 and args.cp_tolerance is None:
+        vjp_active = measure_vjp_active(args, workload, cfg, batch, world, device, barrier, tdt)
+    cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and headline:
         samples = args.cpu_samples or 48 * len(os.sched_getaffinity(0))
         cpu = cpu_baseline_oracle(make_workload(CONFIG_INDEX, samples), samples)
@@ -840,6 +945,7 @@ def main():
             },
             "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms, "postprocess": post_ms},
             "shard_checksums": checksums,
+            "vjp_active": vjp_active,
             "gpu_launches": launches,
             "e2e": {"value": total / (e2e / 1000.0), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e},

@@ -51,7 +51,8 @@
 extern "C" {
 #endif
 
-#define PURIN_CP_ABI_VERSION 2  /* 2: PurinQpForwardArgs gained flags and the resume fields */
+#define PURIN_CP_ABI_VERSION 3  /* 2: PurinQpForwardArgs gained flags and the resume fields;
+                                   3: the adjoint args gained the GMRES work counters */
 
 typedef enum PurinStatus {
   PURIN_OK = 0,
@@ -197,6 +198,12 @@ typedef struct PurinCpAdjointArgs {
   void* linear_residual;    /* out (B,) GMRES residual inf-norm, or NULL     */
   int32_t* device_error;    /* out (1,) 0, or nonzero when a bounded device
                                wait gave up (outputs are then unspecified)   */
+  /* GMRES work actually done, for measurement (NULL to skip; both or neither):
+   * the Arnoldi steps each sample took, and the sum over those steps of the
+   * basis vectors each step orthogonalised against (k at a step that finds
+   * basis vector k + 1).  CGS2 reads 4 k basis vectors at such a step. */
+  int32_t* arnoldi_steps;   /* out (B,) or NULL                              */
+  int64_t* krylov_vectors;  /* out (B,) or NULL                              */
 } PurinCpAdjointArgs;
 
 /* purin_cp_postprocess: bounds.py:247-305 on the unscaled public rows. */
@@ -377,6 +384,8 @@ typedef struct PurinQpAdjointArgs {
   int32_t* linear_status;   /* out (B,) GMRES info 0/1/2, or NULL            */
   void* linear_residual;    /* out (B,) or NULL                              */
   int32_t* device_error;    /* out (1,)                                      */
+  int32_t* arnoldi_steps;   /* out (B,) or NULL, as in PurinCpAdjointArgs    */
+  int64_t* krylov_vectors;  /* out (B,) or NULL                              */
 } PurinQpAdjointArgs;
 
 int32_t purin_qp_forward(const PurinCpPlan* plan, const PurinCpConfig* config,

@@ -13,7 +13,7 @@ from pathlib import Path
 import numpy as np
 
 _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpurin_cp.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 PURIN_FLOAT64, PURIN_FLOAT32 = 0, 1
 OP_FORWARD, OP_ADJOINT, QP_OP_FORWARD, QP_OP_ADJOINT = 0, 1, 2, 3
@@ -63,7 +63,7 @@ class AdjointArgs(ctypes.Structure):
                 ("sample_offset", c_i64), ("total_batch", c_i64), ("grad_values", c_vp),
                 ("grad_rhs", c_vp), ("grad_target", c_vp), ("grad_lower", c_vp),
                 ("grad_upper", c_vp), ("linear_status", c_vp), ("linear_residual", c_vp),
-                ("device_error", c_vp)]
+                ("device_error", c_vp), ("arnoldi_steps", c_vp), ("krylov_vectors", c_vp)]
 
 
 class QpForwardArgs(ctypes.Structure):
@@ -86,7 +86,7 @@ class QpAdjointArgs(ctypes.Structure):
                 ("total_batch", c_i64), ("grad_q", c_vp), ("grad_c", c_vp),
                 ("grad_values", c_vp), ("grad_rhs", c_vp), ("grad_lower", c_vp),
                 ("grad_upper", c_vp), ("linear_status", c_vp), ("linear_residual", c_vp),
-                ("device_error", c_vp)]
+                ("device_error", c_vp), ("arnoldi_steps", c_vp), ("krylov_vectors", c_vp)]
 
 
 class PostArgs(ctypes.Structure):

@@ -20,8 +20,14 @@ PACKAGE = HERE.parent
 ROOT = PACKAGE.parent
 LIB_DIR = PACKAGE / "_lib"
 LIB = LIB_DIR / "libpurin_cp.so"
-SOURCES = ["capi.cu", "cp_forward.cu", "cp_adjoint.cu", "cp_post.cu", "sell_order.cu"]
-HEADERS = ["common.cuh", "plan.cuh", "cp_kernels.cuh", "sell.cuh", "sell_order.h"]
+SOURCES = ["capi.cu", "cp_forward.cu", "cp_adjoint.cu", "cp_gmres_cluster.cu", "cp_post.cu",
+           "sell_order.cu"]
+# cp_forward.cu is also compiled once per (dtype, shared values, QP) combination
+# of its kernels, so that the heavy template instantiations build in parallel.
+FORWARD_PARTS = [(t, sh, qp) for t in ("double", "float") for sh in ("true", "false")
+                 for qp in ("true", "false")]
+HEADERS = ["common.cuh", "plan.cuh", "cp_kernels.cuh", "sell.cuh", "sell_order.h",
+           "adjoint_common.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC",
@@ -52,20 +58,41 @@ def up_to_date() -> bool:
 
 
 def build(verbose: bool = False, force: bool = False) -> Path:
+    """Compile every source to an object in parallel (one nvcc per file), then link."""
+    from concurrent.futures import ThreadPoolExecutor
+    import tempfile
+
     if not force and up_to_date():
         return LIB
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-shared", "-o", str(tmp),
-           *[str(HERE / s) for s in SOURCES]]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    proc = subprocess.run(cmd, cwd=str(HERE), capture_output=True, text=True)
-    if proc.returncode != 0:
-        sys.stderr.write(proc.stdout + proc.stderr)
-        raise RuntimeError("nvcc failed building libpurin_cp.so")
-    if verbose:
-        sys.stderr.write(proc.stdout + proc.stderr)
+    with tempfile.TemporaryDirectory(prefix="purin_build_") as objdir:
+        def compile_one(job):
+            src, defines, stem = job
+            obj = str(Path(objdir) / (stem + ".o"))
+            cmd = [nvcc(), *ARCH, *FLAGS, *defines, "-c", "-o", obj, str(HERE / src)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            return obj, subprocess.run(cmd, cwd=str(HERE), capture_output=True, text=True)
+
+        jobs = [(src, [], Path(src).stem) for src in SOURCES]
+        jobs += [("cp_forward.cu", [f"-DPURIN_FWD_PART_T={t}", f"-DPURIN_FWD_PART_SHARED={sh}",
+                                    f"-DPURIN_FWD_PART_QP={qp}"], f"cp_forward_{t}_{sh}_{qp}")
+                 for t, sh, qp in FORWARD_PARTS]
+        workers = min(len(jobs), max(os.cpu_count() or 1, 1))
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            results = list(pool.map(compile_one, jobs))
+        for _, proc in results:
+            if proc.returncode != 0:
+                sys.stderr.write(proc.stdout + proc.stderr)
+                raise RuntimeError("nvcc failed building libpurin_cp.so")
+            if verbose:
+                sys.stderr.write(proc.stdout + proc.stderr)
+        link = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[obj for obj, _ in results]]
+        proc = subprocess.run(link, cwd=str(HERE), capture_output=True, text=True)
+        if proc.returncode != 0:
+            sys.stderr.write(proc.stdout + proc.stderr)
+            raise RuntimeError("nvcc failed linking libpurin_cp.so")
     os.replace(tmp, LIB)
     return LIB
 

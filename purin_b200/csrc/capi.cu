@@ -202,12 +202,18 @@ struct AdjLayout {
   int R = 1;
   int grid = 0;
   bool smem = true;
+  // GMRES cycles on thread-block clusters holding the Krylov basis on chip: the
+  // cluster size (0: the CTA-per-sample kernel runs the cycles, its basis in the
+  // workspace) and the number of co-resident clusters.
+  int C = 0;
+  int clusters = 0;
   size_t off_x, off_lamp, off_steps, off_dsteps, off_thresh, off_resinf, off_basis, off_gbuf;
   size_t off_ycode, off_dcode, off_counters, counters_bytes, total;
 };
 
 AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
-                       const PurinLinearSolverConfig* lin, int64_t batch, bool qp = false) {
+                       const PurinLinearSolverConfig* lin, int64_t batch, bool qp = false,
+                       int64_t total_batch = 0) {
   AdjLayout L;
   const int n = plan->info.n, m = plan->info.kept_rows;
   const int64_t W = 2 * (int64_t)n + m;
@@ -220,6 +226,33 @@ AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
   L.smem = smem_full + 1024 <= (size_t)plan->max_smem_optin;
   L.grid = f64 ? purin::adjoint_grid<double>(plan->sm_count, n, m, L.R, L.smem, batch)
                : purin::adjoint_grid<float>(plan->sm_count, n, m, L.R, L.smem, batch);
+  // GMRES cycles on clusters that hold the basis on chip, or on the
+  // CTA-per-sample kernel that streams it from HBM.  A cluster step is bound by
+  // latency (barriers across the cluster: config 2 runs about 13 us per Arnoldi
+  // step on 8 SMs), a streaming step by bandwidth shared among all resident
+  // samples; measured on configuration 2 (fp64, 2048 samples) the streaming
+  // kernel takes 150 ms and the clusters 190 ms.  The clusters therefore take
+  // the cycles of a problem whose vectors need the full 256-thread CTA and whose
+  // basis slices fit a cluster of at most 8 CTAs only when the whole batch fits
+  // in one wave of clusters, where the streaming kernel would leave most SMs
+  // idle.  The choice depends on the problem and the GLOBAL batch (the same for
+  // every shard of it), so shards of a batch round alike.
+  // PURIN_CP_GMRES_CLUSTER=0 never uses the clusters, =1 whenever they fit.
+  const char* cl_env = std::getenv("PURIN_CP_GMRES_CLUSTER");
+  const bool cl_off = cl_env && std::string(cl_env) == "0";
+  const bool cl_force = cl_env && std::string(cl_env) == "1";
+  if (!cl_off && purin::adjoint_threads(n, m) == 256) {
+    L.C = f64 ? purin::gmres_cluster_size<double>(n, m, L.R, plan->max_smem_optin)
+              : purin::gmres_cluster_size<float>(n, m, L.R, plan->max_smem_optin);
+    const int64_t global = std::max<int64_t>(total_batch > 0 ? total_batch : batch, 1);
+    if (L.C > 0 && !cl_force && global * L.C > plan->sm_count) L.C = 0;
+    if (L.C > 0) {
+      const int resident = f64 ? purin::gmres_cluster_count<double>(L.C, n, m, L.R)
+                               : purin::gmres_cluster_count<float>(L.C, n, m, L.R);
+      L.clusters = (int)std::min<int64_t>(resident, std::max<int64_t>(batch, 1));
+      if (L.clusters < 1) L.C = 0;
+    }
+  }
   const bool diag = cfg->diagonal_preconditioning && !cfg->accelerated;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -235,7 +268,7 @@ AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
   L.off_dsteps = take(qp ? (size_t)batch * (3 * n + m) * w : diag ? (size_t)batch * (2 * n + m) * w : 0);
   L.off_thresh = take((size_t)batch * w);
   L.off_resinf = take((size_t)batch * w);
-  L.off_basis = take((size_t)std::max(L.grid, 1) * (L.R + 1) * W * w);
+  L.off_basis = take(L.C > 0 ? 0 : (size_t)std::max(L.grid, 1) * (L.R + 1) * W * w);
   L.off_gbuf = take(L.smem ? 0 : (size_t)std::max(L.grid, 1) * (W + n + m) * w);
   L.off_ycode = take((size_t)batch * n);
   L.off_dcode = take((size_t)batch * m);
@@ -457,6 +490,9 @@ purin::AdjParams<T> adjoint_params(const PurinCpPlan* plan, const PurinCpConfig*
   p.lin_status = a->linear_status;
   p.lin_residual = static_cast<T*>(a->linear_residual);
   p.device_error = a->device_error;
+  const bool work = a->arnoldi_steps != nullptr && a->krylov_vectors != nullptr;
+  p.work_steps = work ? a->arnoldi_steps : nullptr;
+  p.work_vectors = work ? reinterpret_cast<long long*>(a->krylov_vectors) : nullptr;
   p.accelerated = cfg->accelerated ? 1 : 0;
   p.diag = (cfg->diagonal_preconditioning && !cfg->accelerated) ? 1 : 0;
   p.norm_iterations = cfg->norm_iterations;
@@ -525,7 +561,7 @@ template <typename T>
 int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                     const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
                     cudaStream_t stream, const QpAdjoint* qp = nullptr) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr);
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -537,6 +573,21 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
   purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
   set_qp(p, qp, cfg);
+  if (L.C > 0) {
+    // Prepare on the CTA-per-sample kernel, every GMRES cycle on the clusters
+    // (one cooperative launch with grid barriers between cycles), then the
+    // pullback; the state passes through the workspace.
+    p.stage = 1;
+    e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch (prepare)");
+    p.stage = 0;
+    e = purin::launch_gmres_cluster<T>(p, L.C, L.clusters, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch (GMRES clusters)");
+    p.stage = 3;
+    e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch (pullback)");
+    return PURIN_OK;
+  }
   e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint launch");
   return PURIN_OK;
@@ -552,7 +603,7 @@ int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, con
                           const PurinCpAdjointArgs* a, int32_t stage, int32_t completed, int32_t* counters,
                           void* workspace, size_t workspace_bytes, cudaStream_t stream,
                           const QpAdjoint* qp = nullptr) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr);
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -584,6 +635,11 @@ int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, con
     p.stage = 3;
     p.cycle_len = nullptr;
     p.cycle_act = nullptr;
+  }
+  if (p.stage == 2 && L.C > 0) {
+    e = purin::launch_gmres_cluster<T>(p, L.C, L.clusters, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage launch (GMRES clusters)");
+    return PURIN_OK;
   }
   e = purin::launch_adjoint<T>(p, L.grid, L.smem, stream);
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint_stage launch");
@@ -754,6 +810,8 @@ int32_t qp_adjoint_call(const PurinCpPlan* plan, const PurinCpConfig* config, co
   a.linear_status = args->linear_status;
   a.linear_residual = args->linear_residual;
   a.device_error = args->device_error;
+  a.arnoldi_steps = args->arnoldi_steps;
+  a.krylov_vectors = args->krylov_vectors;
   if (int32_t r = check_adjoint_args(plan, &a)) return r;
   const QpAdjoint qp{args->q, args->c, args->cot_dual, args->grad_q, args->grad_c};
   const bool f64 = plan->info.dtype == PURIN_FLOAT64;
@@ -1085,7 +1143,11 @@ int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t bat
   }
   if (op == PURIN_CP_OP_ADJOINT || op == PURIN_QP_OP_ADJOINT) {
     if (int32_t r = check_linear(linear)) return r;
-    const AdjLayout L = plan_adjoint(plan, config, linear, batch, op == PURIN_QP_OP_ADJOINT);
+    // The call's choice between the cluster and streaming GMRES kernels depends
+    // on the global batch, which this query does not know: size for the
+    // streaming kernel, whose layout holds every region the other uses.
+    const AdjLayout L = plan_adjoint(plan, config, linear, batch, op == PURIN_QP_OP_ADJOINT,
+                                     INT64_MAX / 2);
     if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
     *bytes = L.total;
     return PURIN_OK;

@@ -1042,13 +1042,55 @@ int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
 
 }  // namespace
 
+// The kernels of one (T, kShared, kQP) combination.  The library compiles this
+// file once per combination with PURIN_FWD_PART_T / _SHARED / _QP defined (those
+// objects instantiate only that combination's kernels, in parallel) and once
+// without, for everything else, which links against the parts.
+template <typename T, bool kShared, bool kQP>
+cudaError_t forward_part_launch(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
+                                cudaStream_t stream);
+template <typename T, bool kShared, bool kQP>
+int forward_part_blocks(int S, int NT, size_t smem_bytes);
+
+#if defined(PURIN_FWD_PART_T)
+
+template <typename T, bool kShared, bool kQP>
+cudaError_t forward_part_launch(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
+                                cudaStream_t stream) {
+  return launch_shared<T, kShared, kQP>(p, S, NT, smem, smem_bytes, stream);
+}
+template <typename T, bool kShared, bool kQP>
+int forward_part_blocks(int S, int NT, size_t smem_bytes) {
+  return blocks_per_sm_shared<T, kShared, kQP>(S, NT, smem_bytes);
+}
+template cudaError_t forward_part_launch<PURIN_FWD_PART_T, PURIN_FWD_PART_SHARED, PURIN_FWD_PART_QP>(
+    const FwdParams<PURIN_FWD_PART_T>&, int, int, bool, size_t, cudaStream_t);
+template int forward_part_blocks<PURIN_FWD_PART_T, PURIN_FWD_PART_SHARED, PURIN_FWD_PART_QP>(int, int,
+                                                                                          size_t);
+
+#else  // the library's other forward functions
+
+#define PURIN_FWD_EXTERN(T, SH, QP)                                                              \
+  extern template cudaError_t forward_part_launch<T, SH, QP>(const FwdParams<T>&, int, int, bool, \
+                                                             size_t, cudaStream_t);              \
+  extern template int forward_part_blocks<T, SH, QP>(int, int, size_t);
+PURIN_FWD_EXTERN(double, true, true)
+PURIN_FWD_EXTERN(double, true, false)
+PURIN_FWD_EXTERN(double, false, true)
+PURIN_FWD_EXTERN(double, false, false)
+PURIN_FWD_EXTERN(float, true, true)
+PURIN_FWD_EXTERN(float, true, false)
+PURIN_FWD_EXTERN(float, false, true)
+PURIN_FWD_EXTERN(float, false, false)
+#undef PURIN_FWD_EXTERN
+
 template <typename T>
 int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, bool qp) {
   if (qp)
-    return shared_values ? blocks_per_sm_shared<T, true, true>(S, NT, smem_bytes)
-                         : blocks_per_sm_shared<T, false, true>(S, NT, smem_bytes);
-  return shared_values ? blocks_per_sm_shared<T, true, false>(S, NT, smem_bytes)
-                       : blocks_per_sm_shared<T, false, false>(S, NT, smem_bytes);
+    return shared_values ? forward_part_blocks<T, true, true>(S, NT, smem_bytes)
+                         : forward_part_blocks<T, false, true>(S, NT, smem_bytes);
+  return shared_values ? forward_part_blocks<T, true, false>(S, NT, smem_bytes)
+                       : forward_part_blocks<T, false, false>(S, NT, smem_bytes);
 }
 
 template <typename T>
@@ -1114,10 +1156,10 @@ template <typename T>
 cudaError_t launch_forward(const FwdParams<T>& p, int S, int NT, bool smem, size_t smem_bytes,
                            cudaStream_t stream) {
   if (p.q_i)
-    return p.vr ? launch_shared<T, true, true>(p, S, NT, smem, smem_bytes, stream)
-                : launch_shared<T, false, true>(p, S, NT, smem, smem_bytes, stream);
-  return p.vr ? launch_shared<T, true, false>(p, S, NT, smem, smem_bytes, stream)
-              : launch_shared<T, false, false>(p, S, NT, smem, smem_bytes, stream);
+    return p.vr ? forward_part_launch<T, true, true>(p, S, NT, smem, smem_bytes, stream)
+                : forward_part_launch<T, false, true>(p, S, NT, smem, smem_bytes, stream);
+  return p.vr ? forward_part_launch<T, true, false>(p, S, NT, smem, smem_bytes, stream)
+              : forward_part_launch<T, false, false>(p, S, NT, smem, smem_bytes, stream);
 }
 
 template cudaError_t launch_forward<double>(const FwdParams<double>&, int, int, bool, size_t,
@@ -1142,5 +1184,7 @@ template cudaError_t permute_rows<double>(const double*, int64_t, const int*, in
                                           cudaStream_t);
 template cudaError_t permute_rows<float>(const float*, int64_t, const int*, int, int64_t, float*,
                                          cudaStream_t);
+
+#endif  // PURIN_FWD_PART_T
 
 }  // namespace purin

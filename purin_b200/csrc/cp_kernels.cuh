@@ -110,6 +110,8 @@ struct AdjParams {
   int32_t* lin_status;
   T* lin_residual;
   int32_t* device_error;
+  int32_t* work_steps;       // (B,) Arnoldi steps taken, or null
+  long long* work_vectors;   // (B,) sum over those steps of the basis vectors, or null
   // General diagonal QP (qp = 1; diagonal_qp.py:133-222): per-sample q and c
   // replace q = 1, c = -target; the dual cotangent enters the right-hand
   // side; q and c get cotangents.
@@ -227,6 +229,20 @@ template <typename T>
 size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors);
 template <typename T>
 int adjoint_grid(int device_sm_count, int n, int m, int R, bool smem_vectors, int64_t batch);
+// Threads per adjoint CTA for a Krylov vector of 2n + m entries (64, 128 or 256).
+int adjoint_threads(int n, int m);
+// GMRES cycles with the Krylov basis in a thread-block cluster's shared memory
+// (cp_gmres_cluster.cu): the smallest cluster size (1, 2, 4 or 8) whose
+// per-CTA slices fit in max_smem_optin bytes, or 0; how many such clusters can
+// be resident at once; and the launch (stage 0: every cycle, cooperative, with
+// grid barriers; stage 2: one cycle).
+template <typename T>
+int gmres_cluster_size(int n, int m, int R, int max_smem_optin);
+template <typename T>
+int gmres_cluster_count(int C, int n, int m, int R);
+template <typename T>
+cudaError_t launch_gmres_cluster(const AdjParams<T>& p, int C, int clusters, cudaStream_t stream);
+
 template <typename T>
 cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors,
                            cudaStream_t stream);

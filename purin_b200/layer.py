@@ -195,6 +195,9 @@ class PreparedChambollePockProjection:
         set_("_total_batch", int(self.batch_size))
         set_("_lockstep_group", None)
         set_("_timers", None)
+        set_("_global_stop", None)
+        set_("_qp_plan", None)
+        set_("last_global_trip", None)
 
     # -- sizes -----------------------------------------------------------------
     @property
@@ -232,6 +235,28 @@ class PreparedChambollePockProjection:
         object.__setattr__(self, "_total_batch", int(total))
         object.__setattr__(self, "_lockstep_group", group)
 
+    def set_global_stop(self, interval: int | None = 100, group=None):
+        """Run the forward under a batch-wide stopping rule, or not (``interval=None``).
+
+        The reference's loop stops when every sample of the batch has been
+        accepted or the budget is spent (``kernels.py:238-240``).  Each sample
+        freezes once accepted, so stopping per sample (the default) gives the same
+        outputs.  With the rule, the forward runs in segments of ``interval``
+        iterations; after each, the samples still running are counted on the
+        device and summed over ``group`` (a ``torch.distributed`` process group
+        whose ranks hold the other shards of the batch: one NCCL all-reduce per
+        segment for CUDA tensors), and every rank stops at the first segment end
+        where none remains anywhere.  The outputs are bit-identical to the
+        default's; ``last_global_trip`` then holds the batch's trip count (the
+        largest iteration count over the global batch), equal on every rank.
+        The segments run the diagonal-QP kernels with q = 1 and c = -target,
+        whose iteration is the distance projection's bit for bit, resuming each
+        sample from the previous segment's state.
+        """
+        if interval is not None and int(interval) < 1:
+            raise ValueError("the global stopping interval must be a positive number of iterations")
+        object.__setattr__(self, "_global_stop", None if interval is None else (int(interval), group))
+
     # -- native calls --------------------------------------------------------------
     def _stream(self):
         return ctypes_stream(torch.cuda.current_stream(self._device))
@@ -262,6 +287,10 @@ class PreparedChambollePockProjection:
 
     def _forward_native(self, data, rhs, target, lower, upper, initial, tolerance, feasible,
                         y, dual, iterations, residual, gap, converged):
+        if self._global_stop is not None:
+            return self._forward_global_stop(data, rhs, target, lower, upper, initial, tolerance,
+                                             feasible, y, dual, iterations, residual, gap,
+                                             converged)
         batch = target.shape[0]
         per_sample = data.shape[0] != 1 and batch != 1
         ws_bytes = self._plan.workspace_size(
@@ -275,6 +304,73 @@ class PreparedChambollePockProjection:
             _ptr(residual), _ptr(gap), _ptr(converged))
         with self._timed("forward"):
             self._plan.forward(self._cfg, args, ws.data_ptr(), ws_bytes, self._stream())
+
+    def _forward_global_stop(self, data, rhs, target, lower, upper, initial, tolerance,
+                             feasible, y, dual, iterations, residual, gap, converged):
+        """The forward under ``set_global_stop``: segments on the QP kernels, outputs in place."""
+        from types import SimpleNamespace
+
+        interval, group = self._global_stop
+        batch, n = target.shape
+        m = self._m
+        dev, dt = target.device, target.dtype
+        if self._qp_plan is None:
+            # The kept rows as a plan whose every row is a CP row (no bound presolve).
+            row_ptr = self._plan.indices(_native.KEPT_ROW_PTR)
+            cols = self._plan.indices(_native.KEPT_COLS)
+            me = self.equality_size
+            object.__setattr__(self, "_qp_plan", _native.Plan(
+                n, me, m - me, row_ptr, cols,
+                _native.PURIN_FLOAT64 if dt == torch.float64 else _native.PURIN_FLOAT32,
+                self._device.index, qp=True))
+        plan = self._qp_plan
+        q = torch.ones((batch, n), dtype=dt, device=dev)
+        c = (-target).contiguous()
+        stride = 0 if data.shape[0] == 1 and batch != 1 else data.shape[1]
+        bounds_stride = 0 if lower.shape[0] == 1 and batch != 1 else n
+        op = _native.QP_OP_FORWARD if stride == 0 else _native.QP_OP_FORWARD_SAMPLE_VALUES
+        cfg = self._cfg
+
+        def segment(end, y0, dual0, ybar0, start):
+            seg_cfg = _native.CpConfig(end, cfg.accelerated, cfg.safety, cfg.norm_iterations,
+                                       cfg.norm_seed, cfg.norm_bound,
+                                       cfg.diagonal_preconditioning, cfg.prng_partitionable)
+            out = SimpleNamespace(
+                y=torch.empty((batch, n), dtype=dt, device=dev),
+                dual=torch.empty((batch, m), dtype=dt, device=dev),
+                ybar=torch.empty((batch, n), dtype=dt, device=dev),
+                iterations=torch.empty((batch,), dtype=torch.int32, device=dev),
+                residual=torch.empty((batch,), dtype=dt, device=dev),
+                gap=torch.empty((batch,), dtype=dt, device=dev),
+                converged=torch.empty((batch,), dtype=torch.uint8, device=dev))
+            y0 = y0.contiguous()
+            dual0 = dual0.contiguous()
+            ybar0 = None if ybar0 is None else ybar0.contiguous()
+            start = None if start is None else start.contiguous()
+            ws_bytes = plan.workspace_size(op, batch, seg_cfg)
+            ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+            args = _native.QpForwardArgs(
+                batch, _ptr(q), _ptr(c), _ptr(data), stride, _ptr(rhs), _ptr(lower), _ptr(upper),
+                bounds_stride, _ptr(y0), _ptr(dual0) if m else None, _ptr(tolerance),
+                self._sample_offset, self._total_batch, _ptr(out.y), _ptr(out.dual),
+                _ptr(out.iterations), _ptr(out.residual), _ptr(out.gap), _ptr(out.converged),
+                _native.QP_NO_VALIDITY, _ptr(ybar0) if ybar0 is not None else None,
+                _ptr(start) if start is not None else None, _ptr(out.ybar))
+            with self._timed("forward"):
+                plan.qp_forward(seg_cfg, args, ws.data_ptr(), ws_bytes, self._stream())
+            return out
+
+        fy, fd, fit, fres, fgap, fconv, trip, _ = lockstep.global_stop_forward(
+            segment, target, initial if m else torch.zeros((batch, 0), dtype=dt, device=dev),
+            batch, int(cfg.max_iterations), interval, group)
+        y.copy_(fy)
+        dual.copy_(fd)
+        iterations.copy_(fit)
+        residual.copy_(fres)
+        gap.copy_(fgap)
+        # converged &= feasible (bounds.py:66), as the projection kernel applies it.
+        converged.copy_(fconv & feasible)
+        object.__setattr__(self, "last_global_trip", trip)
 
     def _adjoint_native(self, data, rhs, target, lower, upper, y, dual, converged, gy, *,
                         need_values, need_rhs, need_target, need_lower, need_upper):
@@ -467,6 +563,8 @@ class _AdjointShard:
         self.lres = empty((batch,))
         self.err = torch.zeros((1,), dtype=torch.int32, device=dev)
         self.counters = torch.zeros((2,), dtype=torch.int32, device=dev)
+        # GMRES work actually done (Arnoldi steps and basis vectors per sample).
+        self.work = (empty((batch,), torch.int32), empty((batch,), torch.int64))
         self.ws_bytes = layer._plan.workspace_size(_native.OP_ADJOINT, batch, layer._cfg,
                                                    layer._lin)
         self.ws = torch.empty((max(self.ws_bytes, 1),), dtype=torch.uint8, device=dev)
@@ -477,13 +575,14 @@ class _AdjointShard:
             0 if lower.shape[0] == 1 and batch != 1 else n, _ptr(y), _ptr(dual), _ptr(converged),
             _ptr(gy), layer._sample_offset, layer._total_batch, _ptr(g_values), _ptr(g_rhs),
             _ptr(g_target), _ptr(g_lower), _ptr(g_upper), _ptr(self.status), _ptr(self.lres),
-            _ptr(self.err))
+            _ptr(self.err), _ptr(self.work[0]), _ptr(self.work[1]))
         # Keep every buffer the arguments point at alive for the shard's lifetime.
         self._inputs = (data, rhs, target, lower, upper, y, dual, converged, gy)
 
     def _done(self):
         layer = self.layer
         object.__setattr__(layer, "_last_linear", (self.status, self.lres))
+        object.__setattr__(layer, "_last_work", self.work)
         if int(self.err.item()) != 0:
             raise RuntimeError("purin_cp_adjoint: a bounded device wait timed out; "
                                "gradients are invalid")

@@ -181,3 +181,88 @@ def test_two_nccl_ranks_reproduce_the_full_batch(tmp_path):
     layer = _layer(problem, cfg, BATCH)
     want = _public_step(layer, theta, target, cot, torch.device(DEV)).cpu().numpy()
     np.testing.assert_array_equal(np.load(out), want)
+
+
+# ---- the cluster-resident GMRES kernel (problems whose basis needs a cluster) -----
+
+def _cluster_case():
+    """Configuration 2's structure (n = 2048, 512 + 1024 rows): its Krylov basis lives in
+    the shared memory of 8-CTA clusters.  CP tolerance 1e-3 so the samples are accepted;
+    GMRES to 1e-5 within 200 steps, which the samples reach in different cycles (the
+    oracle takes 145 steps over 5 cycles)."""
+    from purin_b200 import LinearSolverConfig
+    from purin_b200.workloads import make_workload
+
+    w = make_workload(2, 4)
+    cfg = replace(w.config, tolerance=1e-3,
+                  linear_solver=LinearSolverConfig(tolerance=1e-5, max_iterations=200))
+    cot = np.random.default_rng(11).normal(size=w.candidates.shape)
+    return w.problem, cfg, w.theta, w.candidates, cot
+
+
+@pytest.fixture(scope="module")
+def cluster_case():
+    problem, cfg, theta, target, cot = _cluster_case()
+    oracle = OracleLayer(problem, cfg)
+    _, saved = oracle.solve(target, theta)
+    halves = []
+    for lo, hi in ((0, 2), (2, 4)):
+        _, s = oracle.solve(target[lo:hi], theta[lo:hi], offset=lo, total=4)
+        halves.append((lo, hi, s))
+    return problem, cfg, cot, oracle, saved, halves
+
+
+def test_cluster_gmres_staged_and_sharded_equal_fused(cluster_case):
+    """The cluster kernel's one-cycle launches, driven by the lockstep, equal its fused
+    launch bit for bit, for one shard and for two halves of the batch."""
+    problem, cfg, cot, oracle, saved, halves = cluster_case
+    assert saved["out"].converged.all()
+    layer = _layer(problem, cfg, 4)
+    fused = _shard(layer, oracle, saved, cot)
+    want, want_status, want_res = _numpy(fused.fused(), fused)
+    staged = _shard(layer, oracle, saved, cot)
+    (grads,), completed, cycles = lockstep.run([staged], cfg.linear_solver.max_iterations)
+    got, status, res = _numpy(grads, staged)
+    assert cycles >= 1
+    np.testing.assert_array_equal(status, want_status)
+    np.testing.assert_array_equal(res, want_res)
+    for k in NAMES:
+        np.testing.assert_array_equal(got[k], want[k], err_msg=k)
+    shards = []
+    for lo, hi, s in halves:
+        half = _layer(problem, cfg, hi - lo)
+        half.set_shard(lo, 4)
+        shards.append(_shard(half, oracle, s, cot[lo:hi]))
+    outputs, _, _ = lockstep.run(shards, cfg.linear_solver.max_iterations)
+    parts = [_numpy(g, s) for g, s in zip(outputs, shards)]
+    np.testing.assert_array_equal(np.concatenate([p[1] for p in parts]), want_status)
+    np.testing.assert_array_equal(np.concatenate([p[2] for p in parts]), want_res)
+    for k in NAMES:
+        np.testing.assert_array_equal(np.concatenate([p[0][k] for p in parts]), want[k],
+                                      err_msg=k)
+
+
+def test_cluster_gmres_matches_the_cta_kernel_and_the_oracle(cluster_case, monkeypatch):
+    """The same solves on the CTA-per-sample kernel (PURIN_CP_GMRES_CLUSTER=0) and in the
+    oracle: equal status codes, and gradients within 1e-6 of the largest gradient (GMRES
+    stops at a relative residual of 1e-5, so solves that round differently agree to a
+    fraction of that, not to the last bits)."""
+    problem, cfg, cot, oracle, saved, _ = cluster_case
+    layer = _layer(problem, cfg, 4)
+    shard = _shard(layer, oracle, saved, cot)
+    got, status, _ = _numpy(shard.fused(), shard)
+    monkeypatch.setenv("PURIN_CP_GMRES_CLUSTER", "0")
+    cta = _shard(layer, oracle, saved, cot)
+    ref, ref_status, _ = _numpy(cta.fused(), cta)
+    monkeypatch.delenv("PURIN_CP_GMRES_CLUSTER")
+    stats = {}
+    want = oracle.proj.vjp(saved, cot, stats=stats)
+    np.testing.assert_array_equal(status, ref_status)
+    np.testing.assert_array_equal(status, stats["code"])
+    for k in NAMES:
+        exp = want[k]
+        if k == "values":
+            exp = ell_to_csr(exp, list(oracle.proj.mask.sum(axis=1)))
+        scale = max(float(np.abs(exp).max()), 1e-300)
+        np.testing.assert_allclose(got[k], ref[k], rtol=0, atol=1e-6 * scale, err_msg=k)
+        np.testing.assert_allclose(got[k], exp, rtol=0, atol=1e-6 * scale, err_msg=k)
