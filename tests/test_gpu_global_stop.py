@@ -65,8 +65,8 @@ def test_global_stop_outputs_equal_per_sample_stopping(name, index, batch, dtype
     got, got_gx, got_gt = _step(layer, w, dtype)
     layer.set_global_stop(None)
     for field in FIELDS:
-        np.testing.assert_array_equal(getattr(got, field).cpu().numpy(),
-                                      getattr(want, field).cpu().numpy(), err_msg=field)
+        np.testing.assert_array_equal(getattr(got, field).detach().cpu().numpy(),
+                                      getattr(want, field).detach().cpu().numpy(), err_msg=field)
     np.testing.assert_array_equal(got_gx.cpu().numpy(), want_gx.cpu().numpy())
     np.testing.assert_array_equal(got_gt.cpu().numpy(), want_gt.cpu().numpy())
     assert layer.last_global_trip == int(want.iterations.max())
