@@ -64,6 +64,10 @@ FALLBACK_HBM_GBS = 6650.0
 # ((24.674048 MB + 512 B) / 592); the iterates stay on chip, so the traffic is
 # the per-sample inputs and grows with the batch.
 FORWARD_DRAM_BYTES_PER_SAMPLE = (24.674048e6 + 512.0) / 592
+# The same capture: the L1 data pipe's wavefront rate (the forward's limiter) and
+# the share of shared-memory load wavefronts that are bank conflicts (2.18 G of 5.07 G).
+FORWARD_L1_PIPE_FRAC = 0.778
+FORWARD_BANK_CONFLICT_SHARE = 2.18 / 5.07
 
 
 def parse_args():
@@ -941,7 +945,20 @@ def main():
                 "launch_ms": fwd_ms,
                 "note": "(5n+3m)*8 B per sample-iteration x executed iterations; the iterates "
                         "stay in shared memory, so the HBM stream is the reference layout's "
-                        "traffic, not this kernel's",
+                        "traffic, not this kernel's: HBM is not what bounds it (see "
+                        "roofline_onchip)",
+            },
+            # What does bound the forward kernel: its iterates live in shared memory and
+            # the structure in L2/L1, so its limiter is the L1 data pipe (shared-memory
+            # gathers plus structure loads), from the ncu capture of configuration 2.
+            "roofline_onchip": {
+                "bound": "l1", "kernel": "cp_forward_kernel",
+                "metric": "l1tex__data_pipe_lsu_wavefronts (of peak)",
+                "frac": FORWARD_L1_PIPE_FRAC if index == CONFIG_INDEX else None,
+                "source": "profiles/cp_forward_config2_b592.md (ncu --set full, 592 samples)"
+                if index == CONFIG_INDEX else None,
+                "bank_conflict_share": FORWARD_BANK_CONFLICT_SHARE if index == CONFIG_INDEX
+                else None,
             },
             "kernel_ms": {"forward": fwd_ms, "adjoint": adj_ms, "postprocess": post_ms},
             "shard_checksums": checksums,

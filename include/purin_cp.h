@@ -407,6 +407,118 @@ int32_t purin_qp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* con
                                int32_t completed, int32_t* counters, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* ---- ADMM projection ----------------------------------------------------------
+ * PreparedADMMProjection (src/purin/solvers/admm/solver.py:29-255): OSQP-style
+ * ADMM for min 0.5 x'diag(q)x + c'x s.t. lower <= K x <= upper on a plan from
+ * purin_qp_plan_create (every public row a constraint row, no presolve).
+ *
+ *   purin_admm_forward  <- sparse_admm (admm/kernels.py:43-283) as called by the
+ *                          prepared projection's forward (admm/solver.py:60-97):
+ *                          Jacobi PCG x-updates, or banded Cholesky solves when
+ *                          the band below is given (admm/factor.py:14-105).
+ *   purin_admm_adjoint  <- its bwd (admm/solver.py:175-255): restarted GMRES on
+ *                          the active-set KKT operator, then the pullback to the
+ *                          values, right-hand sides and target.
+ *   purin_admm_adjoint_stage <- the same one phase per call, as
+ *                          purin_cp_adjoint_stage, for shards sharing the batch's
+ *                          GMRES budget.
+ * Row scaling, paired-row compaction (admm/rows.py) and the post-processing of
+ * the unbounded projection (chambolle_pock/solver.py:277-366) stay with the host. */
+
+/* ADMMConfig (admm/config.py:10-40): the fields sparse_admm reads. */
+typedef struct PurinAdmmConfig {
+  double sigma;
+  double alpha;
+  int32_t max_iterations;
+  int32_t cg_max_iterations;
+  int32_t cg_refinement_steps;
+  int32_t check_interval;
+  double cg_tolerance;
+  int32_t adaptive_rho;
+  int32_t rho_update_interval;
+  double rho_update_threshold;
+} PurinAdmmConfig;
+
+/* The banded factor's layout (admm/factor.py:108-144), built by the host in the
+ * reverse Cuthill--McKee order of the row graph: width < 0 selects the PCG path.
+ * Entry k adds penalty[rows[k]] * values[slot_left[k]] * values[slot_right[k]]
+ * (CSR slots) to element destination[k] of the (n, width + 1) lower band. */
+typedef struct PurinAdmmBand {
+  int32_t width;
+  int32_t entries;
+  const int32_t* permutation;  /* device, n */
+  const int32_t* inverse;      /* device, n */
+  const int32_t* rows;         /* device, entries */
+  const int32_t* slot_left;
+  const int32_t* slot_right;
+  const int32_t* destination;
+} PurinAdmmBand;
+
+typedef struct PurinAdmmForwardArgs {
+  int64_t batch;
+  const void* q;            /* (B, n) positive diagonal (ones for the projection) */
+  const void* c;            /* (B, n) linear term (-target for the projection)   */
+  const void* values;       /* CSR slot order of the plan's rows                  */
+  int64_t values_stride;    /* 0 (shared by the batch) or nnz                     */
+  const void* lower;        /* (B, m) row lower bounds (-inf allowed)             */
+  const void* upper;        /* (B, m) row upper bounds                            */
+  const void* penalty;      /* (B, m) initial rho per row                         */
+  const void* tolerance;    /* (B,)                                               */
+  const void* x0;           /* (B, n) warm start                                  */
+  const void* dual0;        /* (B, m) or NULL                                     */
+  PurinAdmmBand band;
+  void* x;                  /* out (B, n)                                         */
+  void* z;                  /* out (B, m)                                         */
+  void* dual;               /* out (B, m)                                         */
+  void* penalty_out;        /* out (B, m) final rho                               */
+  int32_t* iterations;      /* out (B,)                                           */
+  int32_t* inner_iterations;/* out (B,) PCG iterations                            */
+  void* primal_residual;    /* out (B,)                                           */
+  void* dual_residual;      /* out (B,)                                           */
+  void* linear_residual;    /* out (B,)                                           */
+  uint8_t* converged;       /* out (B,)                                           */
+  uint8_t* finite;          /* out (B,)                                           */
+} PurinAdmmForwardArgs;
+
+int32_t purin_admm_workspace_size(const PurinCpPlan* plan, int64_t batch, int32_t band_width,
+                                  size_t* bytes);
+int32_t purin_admm_forward(const PurinCpPlan* plan, const PurinAdmmConfig* config,
+                           const PurinAdmmForwardArgs* args, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* The VJP's inputs: the forward's scaled values and right-hand sides (upper
+ * bounds), its solution and duals, convergence and the cotangent of x. */
+typedef struct PurinAdmmAdjointArgs {
+  int64_t batch;
+  const void* values;
+  int64_t values_stride;
+  const void* rhs;          /* (B, m) scaled right-hand sides                     */
+  const void* y;            /* (B, n) forward solution                            */
+  const void* dual;         /* (B, m) forward duals                               */
+  const uint8_t* converged; /* (B,)                                               */
+  const void* cot_y;        /* (B, n)                                             */
+  double active_tolerance;  /* ADMMConfig.active_tolerance                        */
+  double tolerance;         /* ADMMConfig.tolerance                               */
+  int64_t sample_offset;
+  int64_t total_batch;
+  void* grad_values;        /* out (B, nnz) or NULL                               */
+  void* grad_rhs;           /* out (B, m) or NULL                                 */
+  void* grad_target;        /* out (B, n) or NULL                                 */
+  int32_t* linear_status;   /* out (B,) or NULL                                   */
+  void* linear_residual;    /* out (B,) or NULL                                   */
+  int32_t* device_error;    /* out (1,)                                           */
+} PurinAdmmAdjointArgs;
+
+int32_t purin_admm_adjoint_workspace_size(const PurinCpPlan* plan, int64_t batch,
+                                          const PurinLinearSolverConfig* linear, size_t* bytes);
+int32_t purin_admm_adjoint(const PurinCpPlan* plan, const PurinLinearSolverConfig* linear,
+                           const PurinAdmmAdjointArgs* args, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int32_t purin_admm_adjoint_stage(const PurinCpPlan* plan, const PurinLinearSolverConfig* linear,
+                                 const PurinAdmmAdjointArgs* args, int32_t stage,
+                                 int32_t completed, int32_t* counters, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* purin_cp_forward_noalloc: the forward solve of purin_cp_forward for callers
  * that cannot allocate device memory -- a plugin or custom-call hook that is
  * given only its input and output buffers, a framework that has reserved

@@ -99,12 +99,45 @@ class PostArgs(ctypes.Structure):
                 ("gradient_eligible", c_vp)]
 
 
+class AdmmConfig(ctypes.Structure):
+    _fields_ = [("sigma", c_dbl), ("alpha", c_dbl), ("max_iterations", c_i32),
+                ("cg_max_iterations", c_i32), ("cg_refinement_steps", c_i32),
+                ("check_interval", c_i32), ("cg_tolerance", c_dbl), ("adaptive_rho", c_i32),
+                ("rho_update_interval", c_i32), ("rho_update_threshold", c_dbl)]
+
+
+class AdmmBand(ctypes.Structure):
+    _fields_ = [("width", c_i32), ("entries", c_i32), ("permutation", c_vp), ("inverse", c_vp),
+                ("rows", c_vp), ("slot_left", c_vp), ("slot_right", c_vp),
+                ("destination", c_vp)]
+
+
+class AdmmForwardArgs(ctypes.Structure):
+    _fields_ = [("batch", c_i64), ("q", c_vp), ("c", c_vp), ("values", c_vp),
+                ("values_stride", c_i64), ("lower", c_vp), ("upper", c_vp), ("penalty", c_vp),
+                ("tolerance", c_vp), ("x0", c_vp), ("dual0", c_vp), ("band", AdmmBand),
+                ("x", c_vp), ("z", c_vp), ("dual", c_vp), ("penalty_out", c_vp),
+                ("iterations", c_vp), ("inner_iterations", c_vp), ("primal_residual", c_vp),
+                ("dual_residual", c_vp), ("linear_residual", c_vp), ("converged", c_vp),
+                ("finite", c_vp)]
+
+
+class AdmmAdjointArgs(ctypes.Structure):
+    _fields_ = [("batch", c_i64), ("values", c_vp), ("values_stride", c_i64), ("rhs", c_vp),
+                ("y", c_vp), ("dual", c_vp), ("converged", c_vp), ("cot_y", c_vp),
+                ("active_tolerance", c_dbl), ("tolerance", c_dbl), ("sample_offset", c_i64),
+                ("total_batch", c_i64), ("grad_values", c_vp), ("grad_rhs", c_vp),
+                ("grad_target", c_vp), ("linear_status", c_vp), ("linear_residual", c_vp),
+                ("device_error", c_vp)]
+
+
 EXPORTED = (
     "purin_cp_abi_version", "purin_cp_last_error", "purin_cp_plan_create",
     "purin_cp_plan_destroy", "purin_cp_plan_info", "purin_cp_plan_indices",
     "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_adjoint_stage",
     "purin_cp_postprocess", "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
-    "purin_qp_adjoint_stage",
+    "purin_qp_adjoint_stage", "purin_admm_workspace_size", "purin_admm_forward",
+    "purin_admm_adjoint_workspace_size", "purin_admm_adjoint", "purin_admm_adjoint_stage",
 )
 
 _lib = None
@@ -154,6 +187,20 @@ def load():
                                            ctypes.POINTER(LinearConfig),
                                            ctypes.POINTER(QpAdjointArgs), c_i32, c_i32, c_vp, c_vp,
                                            ctypes.c_size_t, c_vp]
+    lib.purin_admm_workspace_size.argtypes = [c_vp, c_i64, c_i32, ctypes.POINTER(ctypes.c_size_t)]
+    lib.purin_admm_forward.argtypes = [c_vp, ctypes.POINTER(AdmmConfig),
+                                       ctypes.POINTER(AdmmForwardArgs), c_vp, ctypes.c_size_t, c_vp]
+    lib.purin_admm_adjoint_workspace_size.argtypes = [c_vp, c_i64, ctypes.POINTER(LinearConfig),
+                                                      ctypes.POINTER(ctypes.c_size_t)]
+    lib.purin_admm_adjoint.argtypes = [c_vp, ctypes.POINTER(LinearConfig),
+                                       ctypes.POINTER(AdmmAdjointArgs), c_vp, ctypes.c_size_t, c_vp]
+    lib.purin_admm_adjoint_stage.argtypes = [c_vp, ctypes.POINTER(LinearConfig),
+                                             ctypes.POINTER(AdmmAdjointArgs), c_i32, c_i32, c_vp,
+                                             c_vp, ctypes.c_size_t, c_vp]
+    for name in ("purin_admm_workspace_size", "purin_admm_forward",
+                 "purin_admm_adjoint_workspace_size", "purin_admm_adjoint",
+                 "purin_admm_adjoint_stage"):
+        getattr(lib, name).restype = c_i32
     for name in ("purin_cp_plan_create", "purin_cp_plan_destroy", "purin_cp_plan_info",
                  "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward",
                  "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess",
@@ -245,6 +292,36 @@ class Plan:
                                                ctypes.byref(args), stage, completed, counters_ptr,
                                                workspace_ptr, workspace_bytes, stream),
               "purin_qp_adjoint_stage")
+
+    def admm_workspace_size(self, batch, band_width) -> int:
+        size = ctypes.c_size_t()
+        check(self._lib.purin_admm_workspace_size(self.handle, int(batch), int(band_width),
+                                                  ctypes.byref(size)), "purin_admm_workspace_size")
+        return int(size.value)
+
+    def admm_forward(self, cfg, args, workspace_ptr, workspace_bytes, stream):
+        check(self._lib.purin_admm_forward(self.handle, ctypes.byref(cfg), ctypes.byref(args),
+                                           workspace_ptr, workspace_bytes, stream),
+              "purin_admm_forward")
+
+    def admm_adjoint_workspace_size(self, batch, lin) -> int:
+        size = ctypes.c_size_t()
+        check(self._lib.purin_admm_adjoint_workspace_size(self.handle, int(batch), ctypes.byref(lin),
+                                                          ctypes.byref(size)),
+              "purin_admm_adjoint_workspace_size")
+        return int(size.value)
+
+    def admm_adjoint(self, lin, args, workspace_ptr, workspace_bytes, stream):
+        check(self._lib.purin_admm_adjoint(self.handle, ctypes.byref(lin), ctypes.byref(args),
+                                           workspace_ptr, workspace_bytes, stream),
+              "purin_admm_adjoint")
+
+    def admm_adjoint_stage(self, lin, args, stage, completed, counters_ptr, workspace_ptr,
+                           workspace_bytes, stream):
+        check(self._lib.purin_admm_adjoint_stage(self.handle, ctypes.byref(lin), ctypes.byref(args),
+                                                 stage, completed, counters_ptr, workspace_ptr,
+                                                 workspace_bytes, stream),
+              "purin_admm_adjoint_stage")
 
     def postprocess(self, args, stream):
         check(self._lib.purin_cp_postprocess(self.handle, ctypes.byref(args), stream),

@@ -3,8 +3,8 @@
 Mirrors ``src/purin/solvers/api.py:106-141`` (method dispatch and default
 configuration), ``src/purin/solvers/registry.py:10-31`` (third-party
 registration) and ``src/purin/projections/distance.py:9-61``.  This build
-provides the ``chambolle-pock`` method; other PURIN methods can be registered
-with ``register_projection`` and otherwise raise a clear error.
+provides the ``chambolle-pock`` and ``admm`` methods; other PURIN methods can be
+registered with ``register_projection`` and otherwise raise a clear error.
 """
 
 from __future__ import annotations
@@ -14,13 +14,15 @@ from dataclasses import dataclass, replace
 
 import torch
 
-from purin_b200.config import ChambollePockConfig
+from purin_b200.admm import ADMMProjection
+from purin_b200.config import ADMMConfig, ChambollePockConfig
 from purin_b200.layer import ChambollePockProjection
 from purin_b200.types import ProjectionMethod
 
 _REGISTRY: dict[ProjectionMethod, Callable] = {}
 
-_DEFAULT_FACTORIES = {ProjectionMethod.CHAMBOLLE_POCK: ChambollePockProjection}
+_DEFAULT_FACTORIES = {ProjectionMethod.CHAMBOLLE_POCK: ChambollePockProjection,
+                      ProjectionMethod.ADMM: ADMMProjection}
 
 
 def register_projection(method, factory: Callable) -> None:
@@ -39,7 +41,7 @@ def projection_factory(method) -> Callable:
     except KeyError as error:
         raise RuntimeError(
             f"Projection method {selected.value!r} has not been registered; this build "
-            "provides 'chambolle-pock'.") from error
+            "provides 'chambolle-pock' and 'admm'.") from error
 
 
 def registered_methods() -> tuple[str, ...]:
@@ -53,6 +55,8 @@ def prepare_projection(problem, *, method, config=None, batch_size: int, dtype=t
     selected = ProjectionMethod.normalize(method)
     if config is None and selected is ProjectionMethod.CHAMBOLLE_POCK:
         config = ChambollePockConfig()
+    if config is None and selected is ProjectionMethod.ADMM:
+        config = ADMMConfig()
     factory = _DEFAULT_FACTORIES.get(selected)
     if factory is None:
         factory = projection_factory(selected)
@@ -83,11 +87,13 @@ class WeightedDistance:
     config: object = None
 
     def prepare(self, *, batch_size, dtype=torch.float64, backend="cuda"):
-        if ProjectionMethod.normalize(self.method) is not ProjectionMethod.CHAMBOLLE_POCK:
+        method = ProjectionMethod.normalize(self.method)
+        if method not in (ProjectionMethod.CHAMBOLLE_POCK, ProjectionMethod.ADMM):
             if self.method not in ("admm", "primal-dual-interior-point"):
                 raise ValueError("weighted projection supports CP, ADMM, or interior-point")
             raise RuntimeError(f"method {self.method!r} is not part of this build")
-        cfg = self.config or ChambollePockConfig()
+        cfg = self.config or (ADMMConfig() if method is ProjectionMethod.ADMM
+                              else ChambollePockConfig())
         cfg = replace(cfg, metric_diagonal=tuple(float(v) for v in self.diagonal))
         return Distance(self.problem, self.method, cfg).prepare(batch_size=batch_size,
                                                                 dtype=dtype, backend=backend)

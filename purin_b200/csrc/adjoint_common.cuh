@@ -104,6 +104,27 @@ struct Sample {
   const T* sv;
 };
 
+// ADMM (mode 1): the KKT operator and the pullback read the values, the
+// activity codes, y, the duals and the cotangent only.
+template <typename T>
+__device__ Sample<T> make_admm_sample(const AdjParams<T>& p, int64_t X) {
+  {
+    const int n = p.st.n, m = p.st.m;
+    Sample<T> s{};
+    s.vals = p.values + X * p.values_stride;
+    s.rhs = p.rhs + X * m;
+    s.ys = p.y + X * n;
+    s.ds = p.dual + X * m;
+    s.cot = p.cot_y + X * n;
+    s.cotd = nullptr;
+    s.conv = p.converged[X] != 0;
+    s.qp = false;
+    s.dc = p.dcode + X * m;
+    s.yc = p.ycode + X * n;
+    return s;
+  }
+}
+
 template <typename T>
 __device__ Sample<T> make_sample(const AdjParams<T>& p, int64_t X) {
   const int n = p.st.n, m = p.st.m;
@@ -137,6 +158,32 @@ __device__ Sample<T> make_sample(const AdjParams<T>& p, int64_t X) {
     s.av = s.dv = s.sv = nullptr;
   }
   return s;
+}
+
+// ADMM's active-set KKT operator (admm/solver.py:196-206) on z = (v, w):
+// (v + K^T (a w), a K v + (1 - a) w) with a_i = dc[i] in {0, 1}.
+template <typename T>
+__device__ void apply_kkt(const DevStructure& st, const Sample<T>& s, T* buf, T* tn, T* tm) {
+  const int n = st.n, m = st.m;
+  T* zv = buf;
+  T* zw = buf + n;
+  for (int i = threadIdx.x; i < m; i += (int)blockDim.x) tm[i] = T(s.dc[i]) * zw[i];
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) {
+    T acc = T(0);
+    for (int e = st.col_ptr[j]; e < st.col_ptr[j + 1]; ++e)
+      acc = acc + s.vals[st.csc_slot[e]] * tm[st.csc_row[e]];
+    tn[j] = acc;
+  }
+  for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
+    T acc = T(0);
+    for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * zv[st.col[k]];
+    const T a = T(s.dc[i]);
+    zw[i] = a * acc + (T(1) - a) * zw[i];
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x) zv[j] = zv[j] + tn[j];
+  __syncthreads();
 }
 
 // z <- z - J^T z for the packed state z = (y, dual, ybar) (bounds.py:130).

@@ -21,7 +21,7 @@ ROOT = PACKAGE.parent
 LIB_DIR = PACKAGE / "_lib"
 LIB = LIB_DIR / "libpurin_cp.so"
 SOURCES = ["capi.cu", "cp_forward.cu", "cp_adjoint.cu", "cp_gmres_cluster.cu", "cp_post.cu",
-           "sell_order.cu"]
+           "sell_order.cu", "admm_forward.cu"]
 # cp_forward.cu is also compiled once per (dtype, shared values, QP) combination
 # of its kernels, so that the heavy template instantiations build in parallel.
 FORWARD_PARTS = [(t, sh, qp) for t in ("double", "float") for sh in ("true", "false")

@@ -213,10 +213,11 @@ struct AdjLayout {
 
 AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
                        const PurinLinearSolverConfig* lin, int64_t batch, bool qp = false,
-                       int64_t total_batch = 0) {
+                       int64_t total_batch = 0, bool admm = false) {
   AdjLayout L;
   const int n = plan->info.n, m = plan->info.kept_rows;
-  const int64_t W = 2 * (int64_t)n + m;
+  // The CP pullback's state is (y, dual, ybar); ADMM's KKT system is (x, dual).
+  const int64_t W = admm ? (int64_t)n + m : 2 * (int64_t)n + m;
   const size_t w = dtype_size(plan->info.dtype);
   L.R = (int)std::min<int64_t>(std::min<int64_t>(lin->restart, lin->max_iterations), W);
   if (L.R < 1) L.R = 1;
@@ -224,8 +225,8 @@ AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
   const size_t smem_full = f64 ? purin::adjoint_smem_bytes<double>(n, m, L.R, true)
                                : purin::adjoint_smem_bytes<float>(n, m, L.R, true);
   L.smem = smem_full + 1024 <= (size_t)plan->max_smem_optin;
-  L.grid = f64 ? purin::adjoint_grid<double>(plan->sm_count, n, m, L.R, L.smem, batch)
-               : purin::adjoint_grid<float>(plan->sm_count, n, m, L.R, L.smem, batch);
+  L.grid = f64 ? purin::adjoint_grid<double>(plan->sm_count, n, m, L.R, L.smem, batch, admm)
+               : purin::adjoint_grid<float>(plan->sm_count, n, m, L.R, L.smem, batch, admm);
   // GMRES cycles on clusters that hold the basis on chip, or on the
   // CTA-per-sample kernel that streams it from HBM.  A cluster step is bound by
   // latency (barriers across the cluster: config 2 runs about 13 us per Arnoldi
@@ -241,11 +242,11 @@ AdjLayout plan_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg,
   const char* cl_env = std::getenv("PURIN_CP_GMRES_CLUSTER");
   const bool cl_off = cl_env && std::string(cl_env) == "0";
   const bool cl_force = cl_env && std::string(cl_env) == "1";
-  if (!cl_off && purin::adjoint_threads(n, m) == 256) {
+  if (!cl_off && !admm && purin::adjoint_threads(n, m) == 256) {
     L.C = f64 ? purin::gmres_cluster_size<double>(n, m, L.R, plan->max_smem_optin)
               : purin::gmres_cluster_size<float>(n, m, L.R, plan->max_smem_optin);
     const int64_t global = std::max<int64_t>(total_batch > 0 ? total_batch : batch, 1);
-    if (L.C > 0 && !cl_force && global * L.C > plan->sm_count) L.C = 0;
+    if (L.C > 0 && !cl_force && global > plan->sm_count / L.C) L.C = 0;  // no overflow
     if (L.C > 0) {
       const int resident = f64 ? purin::gmres_cluster_count<double>(L.C, n, m, L.R)
                                : purin::gmres_cluster_count<float>(L.C, n, m, L.R);
@@ -557,11 +558,26 @@ void set_qp(purin::AdjParams<T>& p, const QpAdjoint* qp, const PurinCpConfig* cf
   p.norm_bound = cfg->norm_bound ? 1 : 0;
 }
 
+// ADMM's extra adjoint inputs (purin_admm_adjoint): the activity thresholds.
+struct AdmmAdjoint {
+  double active_tolerance;
+  double tolerance;
+};
+
+template <typename T>
+void set_admm(purin::AdjParams<T>& p, const AdmmAdjoint* admm) {
+  if (!admm) return;
+  p.mode = 1;
+  p.act_tol = (T)admm->active_tolerance;
+  p.fwd_tol = (T)admm->tolerance;
+}
+
 template <typename T>
 int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                     const PurinCpAdjointArgs* a, void* workspace, size_t workspace_bytes,
-                    cudaStream_t stream, const QpAdjoint* qp = nullptr) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch);
+                    cudaStream_t stream, const QpAdjoint* qp = nullptr,
+                    const AdmmAdjoint* admm = nullptr) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch, admm != nullptr);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -573,6 +589,7 @@ int32_t run_adjoint(const PurinCpPlan* plan, const PurinCpConfig* cfg, const Pur
   if (e != cudaSuccess) return cuda_fail(e, "purin_cp_adjoint memset");
   purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
   set_qp(p, qp, cfg);
+  set_admm(p, admm);
   if (L.C > 0) {
     // Prepare on the CTA-per-sample kernel, every GMRES cycle on the clusters
     // (one cooperative launch with grid barriers between cycles), then the
@@ -602,8 +619,9 @@ template <typename T>
 int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, const PurinLinearSolverConfig* lin,
                           const PurinCpAdjointArgs* a, int32_t stage, int32_t completed, int32_t* counters,
                           void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                          const QpAdjoint* qp = nullptr) {
-  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch);
+                          const QpAdjoint* qp = nullptr, const AdmmAdjoint* admm = nullptr) {
+  const AdjLayout L = plan_adjoint(plan, cfg, lin, a->batch, qp != nullptr, a->total_batch,
+                                   admm != nullptr);
   if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
   if (workspace == nullptr || workspace_bytes < L.total)
     return fail(PURIN_ERR_WORKSPACE, "adjoint workspace too small: need " + std::to_string(L.total) + " bytes");
@@ -620,6 +638,7 @@ int32_t run_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* cfg, con
   }
   purin::AdjParams<T> p = adjoint_params<T>(plan, cfg, lin, a, L, ws);
   set_qp(p, qp, cfg);
+  set_admm(p, admm);
   unsigned* words = reinterpret_cast<unsigned*>(counters);
   p.barrier = nullptr;
   p.completed0 = completed;
@@ -1296,6 +1315,243 @@ int32_t purin_qp_adjoint_stage(const PurinCpPlan* plan, const PurinCpConfig* con
     return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown adjoint stage");
   return qp_adjoint_call(plan, config, linear, args, stage, completed, counters, workspace, workspace_bytes,
                          stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// ADMM forward workspace: the band factor (when a band is given), then the
+// per-sample vectors of problems too large for shared memory.
+struct AdmmLayout {
+  bool smem = true;
+  size_t off_band = 0, off_state = 0, total = 0;
+};
+
+AdmmLayout plan_admm(const PurinCpPlan* plan, int64_t batch, int32_t width) {
+  AdmmLayout L;
+  const int n = plan->info.n, m = plan->info.kept_rows;
+  const size_t w = dtype_size(plan->info.dtype);
+  const size_t state = (plan->info.dtype == PURIN_FLOAT64 ? purin::admm_state_elems<double>(n, m)
+                                                          : purin::admm_state_elems<float>(n, m)) * w;
+  L.smem = state + 1024 <= (size_t)plan->max_smem_optin;
+  const size_t nb = (size_t)std::max<int64_t>(batch, 0);
+  L.off_band = 0;
+  L.off_state = align_up(width >= 0 ? nb * n * (size_t)(width + 1) * w : 0);
+  L.total = L.off_state + (L.smem ? 0 : align_up(nb * state));
+  return L;
+}
+
+// A CP-config stand-in for the adjoint runners (ADMM's VJP has no CP steps).
+PurinCpConfig admm_cp_config() {
+  PurinCpConfig c{};
+  c.max_iterations = 1;
+  c.safety = 0.5;
+  c.norm_iterations = 1;
+  c.norm_bound = 1;
+  return c;
+}
+
+template <typename T>
+int32_t run_admm(const PurinCpPlan* plan, const PurinAdmmConfig* cfg, const PurinAdmmForwardArgs* a,
+                 void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const AdmmLayout L = plan_admm(plan, a->batch, a->band.width);
+  if (L.total > 0 && (workspace == nullptr || workspace_bytes < L.total))
+    return fail(PURIN_ERR_WORKSPACE, "ADMM workspace too small: need " + std::to_string(L.total) + " bytes");
+  char* ws = static_cast<char*>(workspace);
+  purin::AdmmParams<T> p{};
+  p.st = plan->dev;
+  p.batch = a->batch;
+  p.q = static_cast<const T*>(a->q);
+  p.c = static_cast<const T*>(a->c);
+  p.values = static_cast<const T*>(a->values);
+  p.values_stride = a->values_stride;
+  p.lower = static_cast<const T*>(a->lower);
+  p.upper = static_cast<const T*>(a->upper);
+  p.penalty0 = static_cast<const T*>(a->penalty);
+  p.tolerance = static_cast<const T*>(a->tolerance);
+  p.x0 = static_cast<const T*>(a->x0);
+  p.dual0 = static_cast<const T*>(a->dual0);
+  p.x = static_cast<T*>(a->x);
+  p.z = static_cast<T*>(a->z);
+  p.dual = static_cast<T*>(a->dual);
+  p.penalty = static_cast<T*>(a->penalty_out);
+  p.iterations = a->iterations;
+  p.inner_iterations = a->inner_iterations;
+  p.primal_residual = static_cast<T*>(a->primal_residual);
+  p.dual_residual = static_cast<T*>(a->dual_residual);
+  p.linear_residual = static_cast<T*>(a->linear_residual);
+  p.converged = a->converged;
+  p.finite = a->finite;
+  p.sigma = (T)cfg->sigma;
+  p.alpha = (T)cfg->alpha;
+  p.max_iterations = cfg->max_iterations;
+  p.cg_iterations = cfg->cg_max_iterations;
+  p.refinement_steps = cfg->cg_refinement_steps;
+  p.check_interval = cfg->check_interval;
+  p.cg_tolerance = (T)cfg->cg_tolerance;
+  p.adaptive_rho = cfg->adaptive_rho ? 1 : 0;
+  p.rho_update_interval = cfg->rho_update_interval;
+  p.rho_update_threshold = (T)cfg->rho_update_threshold;
+  p.width = a->band.width;
+  p.nband = a->band.entries;
+  p.band_perm = a->band.permutation;
+  p.band_inv = a->band.inverse;
+  p.band_rows = a->band.rows;
+  p.band_slot_l = a->band.slot_left;
+  p.band_slot_r = a->band.slot_right;
+  p.band_dest = a->band.destination;
+  p.band = a->band.width >= 0 ? reinterpret_cast<T*>(ws + L.off_band) : nullptr;
+  p.gstate = L.smem ? nullptr : reinterpret_cast<T*>(ws + L.off_state);
+  cudaError_t e = purin::launch_admm<T>(p, L.smem, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "purin_admm_forward launch");
+  return PURIN_OK;
+}
+
+int32_t check_admm_plan(const PurinCpPlan* plan) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (plan->info.bound_rows != 0)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "ADMM needs a plan from purin_qp_plan_create");
+  return PURIN_OK;
+}
+
+// ADMM adjoint arguments on the shared runners (stage < 0: fused).
+int32_t admm_adjoint_call(const PurinCpPlan* plan, const PurinLinearSolverConfig* linear,
+                          const PurinAdmmAdjointArgs* args, int32_t stage, int32_t completed,
+                          int32_t* counters, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int32_t r = check_admm_plan(plan)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!args) return fail(PURIN_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (stage >= 0 && stage != PURIN_CP_STAGE_FINISH && !counters)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "counters is NULL");
+  if (stage == PURIN_CP_STAGE_CYCLE && (completed < 0 || completed >= linear->max_iterations))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "completed must lie in [0, max_iterations) for a cycle");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (args->batch == 0) {
+    if (stage < 0 || stage == PURIN_CP_STAGE_FINISH) return PURIN_OK;
+    cudaError_t e = cudaMemsetAsync(counters, 0, 2 * sizeof(int32_t), s);
+    return e == cudaSuccess ? PURIN_OK : cuda_fail(e, "purin_admm_adjoint_stage memset");
+  }
+  const int m = plan->info.kept_rows;
+  if (!args->y || !args->converged || !args->cot_y || (m > 0 && (!args->rhs || !args->dual)) ||
+      (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required ADMM adjoint array is NULL");
+  PurinCpAdjointArgs a{};
+  a.batch = args->batch;
+  a.values = args->values;
+  a.values_stride = args->values_stride;
+  a.rhs = args->rhs;
+  // The CP fields ADMM does not read point at valid arrays of the right size.
+  a.target = args->cot_y;
+  a.lower = args->y;
+  a.upper = args->y;
+  a.bounds_stride = plan->info.n;
+  a.y = args->y;
+  a.dual = args->dual;
+  a.converged = args->converged;
+  a.cot_y = args->cot_y;
+  a.sample_offset = args->sample_offset;
+  a.total_batch = args->total_batch;
+  a.grad_values = args->grad_values;
+  a.grad_rhs = args->grad_rhs;
+  a.grad_target = args->grad_target;
+  a.linear_status = args->linear_status;
+  a.linear_residual = args->linear_residual;
+  a.device_error = args->device_error;
+  if (int32_t r = check_adjoint_args(plan, &a)) return r;
+  const AdmmAdjoint admm{args->active_tolerance, args->tolerance};
+  const PurinCpConfig cfg = admm_cp_config();
+  const bool f64 = plan->info.dtype == PURIN_FLOAT64;
+  if (stage < 0)
+    return f64 ? run_adjoint<double>(plan, &cfg, linear, &a, workspace, workspace_bytes, s, nullptr, &admm)
+               : run_adjoint<float>(plan, &cfg, linear, &a, workspace, workspace_bytes, s, nullptr, &admm);
+  return f64 ? run_adjoint_stage<double>(plan, &cfg, linear, &a, stage, completed, counters, workspace,
+                                         workspace_bytes, s, nullptr, &admm)
+             : run_adjoint_stage<float>(plan, &cfg, linear, &a, stage, completed, counters, workspace,
+                                        workspace_bytes, s, nullptr, &admm);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t purin_admm_workspace_size(const PurinCpPlan* plan, int64_t batch, int32_t band_width,
+                                  size_t* bytes) {
+  if (int32_t r = check_admm_plan(plan)) return r;
+  if (!bytes) return fail(PURIN_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  *bytes = batch == 0 ? 0 : plan_admm(plan, batch, band_width).total;
+  return PURIN_OK;
+}
+
+int32_t purin_admm_forward(const PurinCpPlan* plan, const PurinAdmmConfig* config,
+                           const PurinAdmmForwardArgs* args, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (int32_t r = check_admm_plan(plan)) return r;
+  if (!config || !args) return fail(PURIN_ERR_INVALID_ARGUMENT, "config and args are required");
+  if (config->max_iterations < 1 || config->cg_max_iterations < 1 || config->cg_refinement_steps < 1 ||
+      config->check_interval < 1 || config->rho_update_interval < 1)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "ADMM iteration counts must be positive integers");
+  if (!(config->alpha > 0.0 && config->alpha < 2.0))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "alpha must be between zero and two");
+  if (args->batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  if (args->batch == 0) return PURIN_OK;
+  const int m = plan->info.kept_rows;
+  if (!args->q || !args->c || !args->tolerance || !args->x0 || !args->x || !args->iterations ||
+      !args->inner_iterations || !args->primal_residual || !args->dual_residual ||
+      !args->linear_residual || !args->converged || !args->finite ||
+      (m > 0 && (!args->lower || !args->upper || !args->penalty || !args->z || !args->dual ||
+                 !args->penalty_out)) ||
+      (plan->info.kept_nnz > 0 && !args->values))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a required ADMM forward array is NULL");
+  if (args->values_stride != 0 && args->values_stride != plan->info.kept_nnz)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "values_stride must be 0 or nnz");
+  if (args->band.width > 8)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "the banded factor is used for widths up to 8");
+  if (args->band.width >= 0 && (!args->band.permutation || !args->band.inverse ||
+                                (args->band.entries > 0 && (!args->band.rows || !args->band.slot_left ||
+                                                            !args->band.slot_right ||
+                                                            !args->band.destination))))
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "a banded-factor array is NULL");
+  DeviceGuard guard(plan->info.device);
+  if (!guard.ok) return fail(PURIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return plan->info.dtype == PURIN_FLOAT64 ? run_admm<double>(plan, config, args, workspace, workspace_bytes, s)
+                                           : run_admm<float>(plan, config, args, workspace, workspace_bytes, s);
+}
+
+int32_t purin_admm_adjoint_workspace_size(const PurinCpPlan* plan, int64_t batch,
+                                          const PurinLinearSolverConfig* linear, size_t* bytes) {
+  if (int32_t r = check_admm_plan(plan)) return r;
+  if (int32_t r = check_linear(linear)) return r;
+  if (!bytes) return fail(PURIN_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (batch < 0) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be nonnegative");
+  *bytes = 0;
+  if (batch == 0) return PURIN_OK;
+  DeviceGuard guard(plan->info.device);
+  const PurinCpConfig cfg = admm_cp_config();
+  const AdjLayout L = plan_adjoint(plan, &cfg, linear, batch, false, 0, true);
+  if (L.grid < 1) return fail(PURIN_ERR_UNSUPPORTED, "adjoint kernel cannot be made resident on this device");
+  *bytes = L.total;
+  return PURIN_OK;
+}
+
+int32_t purin_admm_adjoint(const PurinCpPlan* plan, const PurinLinearSolverConfig* linear,
+                           const PurinAdmmAdjointArgs* args, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  return admm_adjoint_call(plan, linear, args, -1, 0, nullptr, workspace, workspace_bytes, stream);
+}
+
+int32_t purin_admm_adjoint_stage(const PurinCpPlan* plan, const PurinLinearSolverConfig* linear,
+                                 const PurinAdmmAdjointArgs* args, int32_t stage, int32_t completed,
+                                 int32_t* counters, void* workspace, size_t workspace_bytes, void* stream) {
+  if (stage != PURIN_CP_STAGE_PREPARE && stage != PURIN_CP_STAGE_CYCLE && stage != PURIN_CP_STAGE_FINISH)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown adjoint stage");
+  return admm_adjoint_call(plan, linear, args, stage, completed, counters, workspace, workspace_bytes,
+                           stream);
 }
 
 int32_t purin_cp_postprocess(const PurinCpPlan* plan, const PurinCpPostArgs* args, void* stream) {

@@ -121,13 +121,82 @@ __device__ void qp_steps(const AdjParams<T>& p, int64_t X, const T* qx, T* base,
   __syncthreads();
 }
 
-template <typename T, bool kSmem>
+template <typename T, bool kAdmm>
+__device__ __forceinline__ Sample<T> sample_of(const AdjParams<T>& p, int64_t X) {
+  if constexpr (kAdmm) return make_admm_sample(p, X);
+  else return make_sample(p, X);
+}
+
+// The adjoint system's operator: the CP pullback (mode 0) or ADMM's KKT operator.
+template <typename T, bool kAdmm>
+__device__ __forceinline__ void apply_any(const DevStructure& st, const Sample<T>& s, T* buf, T* tn,
+                                          T* tm) {
+  if constexpr (kAdmm) apply_kkt(st, s, buf, tn, tm);
+  else apply_operator(st, s, buf, tn, tm);
+}
+
+// Threshold and initial residual of an ADMM sample's system (x = 0).
+template <typename T>
+__device__ void admm_initial_residual(const AdjParams<T>& p, const DevStructure& st, const Sample<T>& s,
+                                      int64_t X, int W, T* buf, T* tn, T* tm, T* red) {
+  const int n = st.n, m = st.m;
+  const T zero = T(0);
+  T gmax = zero;
+  for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
+    gmax = pmax(gmax, fabs(rhs_entry(s, n, m, e)));
+    buf[e] = zero;
+    p.x[X * W + e] = zero;
+  }
+  gmax = block_max(gmax, red);
+  apply_kkt(st, s, buf, tn, tm);
+  T r0 = zero;
+  for (int e = threadIdx.x; e < W; e += (int)blockDim.x) r0 = pmax(r0, fabs(rhs_entry(s, n, m, e) - buf[e]));
+  r0 = block_max(r0, red);
+  if (threadIdx.x == 0) {
+    const T thr = pmax(p.lin_atol, p.lin_tol * gmax);
+    p.thresh[X] = thr;
+    p.resinf[X] = r0;
+    if (r0 > thr) atomicAdd(&p.cycle_act[0], 1u);
+  }
+  __syncthreads();
+}
+
+// ADMM's pullback (admm/solver.py:236-255) of the validated adjoint x = (v, w):
+// target -> v, rhs -> a w, values -> -(dual_i v_j + a_i w_i y_j) on the support.
+template <typename T>
+__device__ void admm_pullback(const AdjParams<T>& p, const DevStructure& st, const Sample<T>& s,
+                              int64_t X, const T* x, bool valid, int code, T ri) {
+  const int n = st.n, m = st.m;
+  const T zero = T(0);
+  for (int j = threadIdx.x; j < n; j += (int)blockDim.x)
+    if (p.g_target) p.g_target[X * n + j] = valid ? clean(x[j]) : zero;
+  for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
+    const T wi = valid ? T(s.dc[i]) * x[n + i] : zero;
+    if (p.g_rhs) p.g_rhs[X * m + i] = clean(wi);
+    if (p.g_values) {
+      const T di = s.ds[i];
+      T* gv = p.g_values + X * st.nnz;
+      for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) {
+        const int j = st.col[k];
+        const T vj = valid ? x[j] : zero;
+        gv[k] = clean(-(di * vj + wi * s.ys[j]));
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (p.lin_status) p.lin_status[X] = code;
+    if (p.lin_residual) p.lin_residual[X] = ri;
+  }
+  __syncthreads();
+}
+
+template <typename T, bool kSmem, bool kAdmm>
 __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T> p) {
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ int s_flag;
   const DevStructure& st = p.st;
   const int n = st.n, m = st.m, me = st.me;
-  const int W = 2 * n + m;
+  const int W = kAdmm ? n + m : 2 * n + m;
   const int R = p.R;
   T* sm = reinterpret_cast<T*>(dyn);
   T *buf, *tn, *tm, *small;
@@ -171,6 +240,21 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         p.thresh[X] = pmax(p.lin_atol, zero);
         p.resinf[X] = zero;
       }
+      continue;
+    }
+    if constexpr (kAdmm) {
+      // ADMM (admm/solver.py:184-194): rows active where equality, or where the
+      // dual is positive and the slack rhs - K y is tight.
+      const Sample<T> s = sample_of<T, kAdmm>(p, X);
+      for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
+        T acc = zero;
+        for (int k = st.row_ptr[i]; k < st.row_ptr[i + 1]; ++k) acc = acc + s.vals[k] * s.ys[st.col[k]];
+        const T slack = s.rhs[i] - acc;
+        const bool act = i < me || (s.ds[i] > p.act_tol && slack <= pmax(p.act_tol, p.fwd_tol));
+        s.dc[i] = act ? 1 : 0;
+      }
+      __syncthreads();
+      admm_initial_residual(p, st, s, X, W, buf, tn, tm, red);
       continue;
     }
     const T* vals = p.values + X * p.values_stride;
@@ -253,7 +337,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       }
     }
     __syncthreads();
-    const Sample<T> s = make_sample(p, X);
+    const Sample<T> s = sample_of<T, kAdmm>(p, X);
     // Linearisation point (y*, lambda*, ybar = y*): lambda+ and derivative codes.
     for (int i = threadIdx.x; i < m; i += (int)blockDim.x) {
       T acc = zero;
@@ -323,12 +407,12 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
     for (int64_t X = blockIdx.x; X < p.batch; X += gridDim.x) {
       const T thr = p.thresh[X];
       if (!(p.resinf[X] > thr)) continue;  // not cycle-active: frozen
-      const Sample<T> s = make_sample(p, X);
+      const Sample<T> s = sample_of<T, kAdmm>(p, X);
       T* x = p.x + X * W;
       // residual = g - A x, normalised into V[0]
       for (int e = threadIdx.x; e < W; e += (int)blockDim.x) buf[e] = x[e];
       __syncthreads();
-      apply_operator(st, s, buf, tn, tm);
+      apply_any<T, kAdmm>(st, s, buf, tn, tm);
       T ss = zero;
       for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
         const T r = rhs_entry(s, n, m, e) - buf[e];
@@ -349,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       __syncthreads();
       int it = 0;
       while (it < limit && s_flag) {
-        apply_operator(st, s, buf, tn, tm);
+        apply_any<T, kAdmm>(st, s, buf, tn, tm);
         basis_dots(V, W, buf, it + 1, coef, red);
         basis_update(V, W, buf, it + 1, coef);
         basis_dots(V, W, buf, it + 1, c2, red);
@@ -383,7 +467,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
         x[e] = cand;
       }
       __syncthreads();
-      apply_operator(st, s, buf, tn, tm);
+      apply_any<T, kAdmm>(st, s, buf, tn, tm);
       T cn = zero;
       for (int e = threadIdx.x; e < W; e += (int)blockDim.x) cn = pmax(cn, fabs(rhs_entry(s, n, m, e) - buf[e]));
       cn = block_max(cn, red);
@@ -430,7 +514,7 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       }
       continue;
     }
-    const Sample<T> s = make_sample(p, X);
+    const Sample<T> s = sample_of<T, kAdmm>(p, X);
     const T* x = p.x + X * W;
     int fin = 1;
     for (int e = threadIdx.x; e < W; e += (int)blockDim.x) {
@@ -448,6 +532,10 @@ __global__ void __launch_bounds__(kThreads) cp_adjoint_kernel(const AdjParams<T>
       for (int e = threadIdx.x; e < W; e += (int)blockDim.x) buf[e] = zero;
     }
     __syncthreads();
+    if constexpr (kAdmm) {
+      admm_pullback(p, st, s, X, buf, valid, code, ri);
+      continue;
+    }
     const T* zy = buf;
     const T* zd = buf + n;
     const T* zb = buf + n + m;
@@ -530,27 +618,28 @@ size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors) {
   return elems * sizeof(T);
 }
 
-template <typename T>
-int adjoint_grid(int sm_count, int n, int m, int R, bool smem_vectors, int64_t batch) {
-  const size_t smem = adjoint_smem_bytes<T>(n, m, R, smem_vectors);
-  const int threads = adjoint_threads(n, m);
+template <typename T, bool kSmem, bool kAdmm>
+int adjoint_grid_k(int sm_count, int threads, size_t smem, int64_t batch) {
+  auto kern = cp_adjoint_kernel<T, kSmem, kAdmm>;
   int per_sm = 0;
-  if (smem_vectors) {
-    auto kern = cp_adjoint_kernel<T, true>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
-      return 0;
-  } else {
-    auto kern = cp_adjoint_kernel<T, false>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
-      return 0;
-  }
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
+    return 0;
   int64_t grid = (int64_t)per_sm * sm_count;
   if (grid > batch) grid = batch;
   return (int)grid;
+}
+
+template <typename T>
+int adjoint_grid(int sm_count, int n, int m, int R, bool smem_vectors, int64_t batch, bool admm) {
+  const size_t smem = adjoint_smem_bytes<T>(n, m, R, smem_vectors);
+  const int threads = adjoint_threads(n, m);
+  if (admm)
+    return smem_vectors ? adjoint_grid_k<T, true, true>(sm_count, threads, smem, batch)
+                        : adjoint_grid_k<T, false, true>(sm_count, threads, smem, batch);
+  return smem_vectors ? adjoint_grid_k<T, true, false>(sm_count, threads, smem, batch)
+                      : adjoint_grid_k<T, false, false>(sm_count, threads, smem, batch);
 }
 
 template <typename T>
@@ -558,7 +647,9 @@ cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors, c
   const int n = p.st.n, m = p.st.m;
   const size_t smem = adjoint_smem_bytes<T>(n, m, p.R, smem_vectors);
   void* args[] = {(void*)&p};
-  auto kern = smem_vectors ? cp_adjoint_kernel<T, true> : cp_adjoint_kernel<T, false>;
+  const bool admm = p.mode == 1;
+  auto kern = admm ? (smem_vectors ? cp_adjoint_kernel<T, true, true> : cp_adjoint_kernel<T, false, true>)
+                   : (smem_vectors ? cp_adjoint_kernel<T, true, false> : cp_adjoint_kernel<T, false, false>);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int threads = adjoint_threads(n, m);
@@ -570,8 +661,8 @@ cudaError_t launch_adjoint(const AdjParams<T>& p, int grid, bool smem_vectors, c
 
 template size_t adjoint_smem_bytes<double>(int, int, int, bool);
 template size_t adjoint_smem_bytes<float>(int, int, int, bool);
-template int adjoint_grid<double>(int, int, int, int, bool, int64_t);
-template int adjoint_grid<float>(int, int, int, int, bool, int64_t);
+template int adjoint_grid<double>(int, int, int, int, bool, int64_t, bool);
+template int adjoint_grid<float>(int, int, int, int, bool, int64_t, bool);
 template cudaError_t launch_adjoint<double>(const AdjParams<double>&, int, bool, cudaStream_t);
 template cudaError_t launch_adjoint<float>(const AdjParams<float>&, int, bool, cudaStream_t);
 

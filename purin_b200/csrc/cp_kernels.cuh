@@ -122,6 +122,12 @@ struct AdjParams {
   T* g_q;             // (B, n) or null
   T* g_c;             // (B, n) or null
   int norm_bound;     // QP backward only: L from |K| row/column sums
+  // ADMM projection (mode 1; admm/solver.py:175-255): GMRES on the active-set KKT
+  // operator [v + K^T (a w); a K v + (1 - a) w] of n + m unknowns, with the
+  // activity a of each row from the forward's duals and slacks.
+  int mode;
+  T act_tol;          // ADMMConfig.active_tolerance
+  T fwd_tol;          // ADMMConfig.tolerance
   // configuration
   int accelerated;
   int diag;
@@ -186,6 +192,60 @@ struct PostParams {
   uint8_t* elig;
 };
 
+// ADMM forward (admm_forward.cu): sparse_admm (src/purin/solvers/admm/kernels.py:43-283)
+// of one sample per CTA over a plan whose rows are all constraint rows.
+template <typename T>
+struct AdmmParams {
+  DevStructure st;
+  int64_t batch;
+  const T* q;            // (B, n) positive diagonal objective
+  const T* c;            // (B, n) linear objective
+  const T* values;       // CSR slot order, stride values_stride (0: shared)
+  int64_t values_stride;
+  const T* lower;        // (B, m)
+  const T* upper;        // (B, m)
+  const T* penalty0;     // (B, m) initial rho per row
+  const T* tolerance;    // (B,)
+  const T* x0;           // (B, n) warm start (z0 = clip(K x0))
+  const T* dual0;        // (B, m) or null
+  // outputs
+  T* x;
+  T* z;
+  T* dual;
+  T* penalty;            // final rho
+  int32_t* iterations;
+  int32_t* inner_iterations;
+  T* primal_residual;
+  T* dual_residual;
+  T* linear_residual;
+  uint8_t* converged;
+  uint8_t* finite;
+  // configuration (ADMMConfig, admm/config.py:10-40)
+  T sigma, alpha;
+  int max_iterations, cg_iterations, refinement_steps, check_interval;
+  T cg_tolerance;
+  int adaptive_rho, rho_update_interval;
+  T rho_update_threshold;
+  // Banded factor (admm/factor.py): width < 0 means the PCG path.  Entries k
+  // add penalty[rows[k]] * values[slot_l[k]] * values[slot_r[k]] to
+  // band[dest[k]] of the (n, width + 1) lower band in the permuted order.
+  int width;
+  int nband;
+  const int* band_perm;
+  const int* band_inv;
+  const int* band_rows;
+  const int* band_slot_l;
+  const int* band_slot_r;
+  const int* band_dest;
+  T* band;               // workspace: B * n * (width + 1)
+  T* gstate;             // per-CTA vectors when they do not fit in shared memory
+};
+
+template <typename T>
+size_t admm_state_elems(int n, int m);
+template <typename T>
+cudaError_t launch_admm(const AdmmParams<T>& p, bool smem, cudaStream_t stream);
+
 // Threads per forward CTA; one-sample tiles whose state leaves room for only one
 // or two CTAs of kForwardThreads per SM run 2 x or 4 x (kWideThreads) as many.
 constexpr int kForwardThreads = 256;
@@ -228,7 +288,8 @@ cudaError_t permute_rows(const T* src, int64_t src_stride, const int* perm, int 
 template <typename T>
 size_t adjoint_smem_bytes(int n, int m, int R, bool smem_vectors);
 template <typename T>
-int adjoint_grid(int device_sm_count, int n, int m, int R, bool smem_vectors, int64_t batch);
+int adjoint_grid(int device_sm_count, int n, int m, int R, bool smem_vectors, int64_t batch,
+                 bool admm = false);
 // Threads per adjoint CTA for a Krylov vector of 2n + m entries (64, 128 or 256).
 int adjoint_threads(int n, int m);
 // GMRES cycles with the Krylov basis in a thread-block cluster's shared memory

@@ -50,6 +50,27 @@ REFERENCE_CASES = {
         "source": "tests/test_regression_cp_bound_presolve.py:13-27",
         "target": [[-3.0, 4.0]], "y": [[0.0, 1.0]],
         "multipliers_ineq": [[1.5, 0.75, 0.0, 3.0]], "slacks": [[0.0, 0.0, 2.0, 0.0]]},
+    "admm_affine_projection": {
+        "source": "tests/test_regression_admm.py:16-57",
+        "target": [[2.0, 0.0], [-2.0, 0.0]], "parameters": [[1.0], [1.0]],
+        "y": [[1.5, -0.5], [0.0, 1.0]], "jacobian_sample0": [[0.5, -0.5], [-0.5, 0.5]],
+        "jacobian_sample1": [[0.0, 0.0], [0.0, 0.0]], "theta_derivative": [[0.5, 0.5], [0.0, 1.0]],
+        "atol": 1e-8},
+    "admm_two_sided_box": {
+        "source": "tests/test_regression_admm_rows.py:12-40",
+        "target": [[3.0, 4.0], [-2.0, -3.0], [0.5, 0.5]], "kept_rows": 2,
+        "y": [[1.0, 2.0], [0.0, -1.0], [0.5, 0.5]],
+        "multipliers_ineq": [[2.0, 0.0, 2.0, 0.0], [0.0, 2.0, 0.0, 2.0], [0.0, 0.0, 0.0, 0.0]],
+        "slacks": [[0.0, 1.0, 0.0, 3.0], [1.0, 0.0, 3.0, 0.0], [0.5, 0.5, 1.5, 1.5]],
+        "gradient_of_sum": [[0.0, 0.0], [0.0, 0.0], [1.0, 1.0]], "atol": 2e-9},
+    "admm_periodic_acceptance": {
+        "source": "tests/test_regression_admm_diagnostics.py:15-44",
+        "target": [[3.0, -1.0], [-2.0, 2.0], [0.2, 0.4]],
+        "y": [[1.0, 0.0], [0.0, 1.0], [0.4, 0.6]], "atol": 3e-9},
+    "admm_parameter_dependent_active_inequality": {
+        "source": "tests/test_regression_admm.py:162-180",
+        "target": [[-2.0, 0.3]], "parameters": [[1.0]], "y": [[1.0, 0.3]],
+        "theta_jacobian": [1.0, 0.0], "atol": 1e-8},
     "parameter_dependent_bound": {
         "source": "tests/test_regression_cp_bound_presolve.py:30-53",
         "target": [[3.0]], "parameters": [[2.0, 1.0]], "y": [[0.5]],

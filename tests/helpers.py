@@ -137,3 +137,47 @@ def random_theta(rng, mats, batch, slack=0.1):
     b = (A_eq @ x0.T).T
     h = (A_in @ x0.T).T + rng.uniform(0.0, slack, (batch, A_in.shape[0]))
     return np.concatenate([b, h], axis=1)
+
+
+class OracleADMMLayer:
+    """A problem + ADMMConfig evaluated by the ADMM oracle (values from the product frontend)."""
+
+    def __init__(self, problem, cfg, dtype=np.float64):
+        from oracle.admm import OracleADMMConfig, OracleADMMProjection
+
+        self.canonical = canonical_of(problem)
+        self.cfg = cfg
+        self.dtype = np.dtype(dtype)
+        c = self.canonical
+        lin = cfg.linear_solver
+        ocfg = OracleADMMConfig(
+            tolerance=cfg.tolerance, max_iterations=cfg.max_iterations, rho=cfg.rho,
+            sigma=cfg.sigma, alpha=cfg.alpha, equality_rho_multiplier=cfg.equality_rho_multiplier,
+            cg_max_iterations=cfg.cg_max_iterations, cg_tolerance=cfg.cg_tolerance,
+            cg_refinement_steps=cfg.cg_refinement_steps, adaptive_rho=cfg.adaptive_rho,
+            rho_update_interval=cfg.rho_update_interval,
+            rho_update_threshold=cfg.rho_update_threshold, row_scaling=cfg.row_scaling,
+            active_tolerance=cfg.active_tolerance, check_interval=cfg.check_interval,
+            linear_tolerance=lin.tolerance, linear_atol=lin.atol, linear_restart=lin.restart,
+            linear_max_iterations=lin.max_iterations,
+            adjoint_tolerance=cfg.implicit_gradient.adjoint_tolerance)
+        zero = np.zeros((1, c.parameter_size))
+        values0, _ = c.evaluate(zero)
+        ell0 = to_ell(c, np.asarray(values0, np.float64))[0]
+        self.proj = OracleADMMProjection(c.equality_sparsity, c.inequality_sparsity,
+                                         c.variable_size, ocfg, values_at_zero=ell0)
+
+    def arrays(self, theta, batch):
+        theta = np.zeros((batch, 0), self.dtype) if theta is None else np.asarray(theta, self.dtype)
+        values, rhs = self.canonical.evaluate(theta)
+        values = np.broadcast_to(values, (batch, values.shape[1])).astype(self.dtype)
+        rhs = np.broadcast_to(rhs, (batch, rhs.shape[1])).astype(self.dtype)
+        return to_ell(self.canonical, values), rhs
+
+    def solve(self, target, theta=None, multipliers_eq=None, multipliers_ineq=None):
+        target = np.asarray(target, self.dtype)
+        values, rhs = self.arrays(theta, target.shape[0])
+        return self.proj.solve(values, rhs, target, multipliers_eq, multipliers_ineq)
+
+    def __call__(self, target, theta=None):
+        return self.solve(target, theta)[0]["y"]

@@ -266,3 +266,31 @@ def test_cluster_gmres_matches_the_cta_kernel_and_the_oracle(cluster_case, monke
         scale = max(float(np.abs(exp).max()), 1e-300)
         np.testing.assert_allclose(got[k], ref[k], rtol=0, atol=1e-6 * scale, err_msg=k)
         np.testing.assert_allclose(got[k], exp, rtol=0, atol=1e-6 * scale, err_msg=k)
+
+
+def test_workspace_query_covers_either_gmres_kernel(monkeypatch):
+    """The adjoint workspace a layer sizes before the call (purin_cp_workspace_size, which
+    does not know the global batch) must cover the GMRES kernel the call then picks: the
+    streaming kernel for a batch beyond one wave of clusters (fp32 configuration 4, 32
+    samples, 8-CTA clusters), the clusters when forced.  Both give the same status codes
+    and gradients to GMRES's accuracy."""
+    from purin_b200 import LinearSolverConfig
+    from purin_b200.workloads import make_workload
+
+    w = make_workload(4, 32)
+    cfg = replace(w.config, tolerance=0.5, linear_solver=LinearSolverConfig(tolerance=1e-4))
+    layer = prepare_projection(w.problem, method="chambolle-pock", config=cfg, batch_size=32,
+                               dtype=torch.float32, backend=DEV)
+    grads, codes = [], []
+    for mode in ("", "1"):
+        if mode:
+            monkeypatch.setenv("PURIN_CP_GMRES_CLUSTER", mode)
+        x = _t(w.candidates, torch.float32).requires_grad_(True)
+        y = layer(x, _t(w.theta, torch.float32))
+        ((y - _t(w.targets, torch.float32)) ** 2).sum().backward()
+        grads.append(x.grad.cpu().numpy())
+        codes.append(layer._last_linear[0].cpu().numpy())
+    np.testing.assert_array_equal(codes[0], codes[1])
+    assert (codes[0] == 0).any()
+    scale = float(np.abs(grads[0]).max())
+    np.testing.assert_allclose(grads[1], grads[0], rtol=0, atol=1e-3 * scale)
