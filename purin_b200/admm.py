@@ -281,8 +281,8 @@ class PreparedADMMProjection:
         """K x with each row summed in slot order: values (1|B, nnz), x (B, n)."""
         if self._m == 0:
             return torch.zeros((x.shape[0], 0), dtype=x.dtype, device=x.device)
-        vals = torch.cat([values, torch.zeros_like(values[:, :1])], dim=1)
-        xp = torch.cat([x, torch.zeros_like(x[:, :1])], dim=1)
+        pad = lambda t: torch.cat([t, t.new_zeros((t.shape[0], 1))], dim=1)
+        vals, xp = pad(values), pad(x)
         cols = torch.cat([self._cols, torch.full_like(self._cols[:1], self.output_size)])
         acc = None
         for k in range(self._row_ell.shape[1]):
@@ -293,8 +293,8 @@ class PreparedADMMProjection:
 
     def _tmv(self, values, w):
         """K^T w with each column summed in ascending row order."""
-        vals = torch.cat([values, torch.zeros_like(values[:, :1])], dim=1)
-        wp = torch.cat([w, torch.zeros_like(w[:, :1])], dim=1)
+        pad = lambda t: torch.cat([t, t.new_zeros((t.shape[0], 1))], dim=1)
+        vals, wp = pad(values), pad(w)
         acc = torch.zeros((w.shape[0], self.output_size), dtype=w.dtype, device=w.device)
         for k in range(self._col_slots.shape[1]):
             acc = acc + vals[:, self._col_slots[:, k]] * wp[:, self._col_rows[:, k]]

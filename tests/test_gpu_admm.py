@@ -157,7 +157,7 @@ def test_random_problems_match_the_oracle(seed, adaptive, interval):
     # Converged-mode iteration counts within 2 % (acceptance is tested on rounding-
     # dependent residuals; with a check interval of 25 the counts coincide).
     counts, expected = out.iterations.cpu().numpy(), want["iterations"]
-    assert np.all(np.abs(counts - expected) <= np.maximum(0.02 * expected, 0)), (counts, expected)
+    assert np.all(np.abs(counts - expected) <= np.maximum(0.02 * expected, 1)), (counts, expected)
     cot = np.random.default_rng(100 + seed).normal(size=target.shape)
     (out.y * _t(cot)).sum().backward()
     grads = oracle.proj.vjp(saved, cot)
