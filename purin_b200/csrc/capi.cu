@@ -122,7 +122,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const size_t cap = (size_t)plan->max_smem_optin;
   const int64_t sms = std::max(1, plan->sm_count);
   // PURIN_CP_SAMPLES_PER_TILE (1, 2, 4 or 8) overrides the tile width when it
-  // fits, PURIN_CP_TILE_THREADS (256, 512 or 1024; 128 for QP plans) the
+  // fits, PURIN_CP_TILE_THREADS (256, 512, 768 or 1024; 128 for QP plans) the
   // threads per CTA.
   int forced = 0, forced_threads = 0;
   if (const char* env = std::getenv("PURIN_CP_SAMPLES_PER_TILE")) forced = std::atoi(env);
@@ -130,19 +130,22 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   // Default: the shape whose resident CTAs hold the most warps over the batch
   // (the iteration is latency-bound), then the most samples, then the first of
   // this list.  Every shape whose state fits in shared memory is a candidate.
-  static const int kShapes[7][2] = {{1, purin::kForwardThreads}, {2, purin::kForwardThreads},
-                                    {4, purin::kForwardThreads}, {8, purin::kForwardThreads},
-                                    {1, 2 * purin::kForwardThreads}, {1, purin::kWideThreads},
-                                    {1, purin::kNarrowThreads}};
+  // Shapes from index kFirstWideShape on are the wide multi-sample tiles.
+  static const int kShapes[kForwardShapeCount][2] = {
+      {1, purin::kForwardThreads},     {2, purin::kForwardThreads}, {4, purin::kForwardThreads},
+      {8, purin::kForwardThreads},     {1, 2 * purin::kForwardThreads}, {1, purin::kWideThreads},
+      {1, purin::kNarrowThreads},      {2, 512}, {4, 512}, {2, 768}, {4, 768}, {2, 1024}, {4, 1024}};
+  constexpr int kFirstWideShape = 7;
   // The narrow QP tile only where a sample's vectors give its 128 threads at
   // most 4 entries each: larger samples keep the 256-thread tile's parallelism.
   const bool narrow_ok = qp && (int64_t)n_pos + m_pos <= 4 * purin::kNarrowThreads;
   int best = -1;
   int64_t best_warps = -1, best_samples = -1;
   int pair_blocks = 0;  // resident CTAs per SM of the two-sample 256-thread tile (shape 1)
-  for (int k = 0; k < 7; ++k) {
+  for (int k = 0; k < kForwardShapeCount; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
     if (qp && S != 1) continue;  // the QP kernels are built for one-sample tiles
+    if (k >= kFirstWideShape && forced == 0 && forced_threads == 0) continue;  // forced only
     if (NT == purin::kNarrowThreads && !(narrow_ok || (qp && forced_threads == NT))) continue;
     const size_t stat = f64 ? purin::forward_static_smem<double>(S, NT)
                             : purin::forward_static_smem<float>(S, NT);
@@ -181,6 +184,38 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   if (!f64 && best >= 0 && forced == 0 && forced_threads == 0 && pair_blocks >= 2 &&
       (batch + 1) / 2 >= sms * pair_blocks && kShapes[best][0] == 1)
     best = 1;
+  // A structure far larger than the L1 beside the tile state streams from L2
+  // once per tile-iteration (value plus 16-bit index per stored entry, both
+  // products).  A wide tile of 4 (else 2) samples on 768 threads shares that
+  // stream among its samples and keeps 24 warps.  Configuration 4 (n = 4096,
+  // m = 3072, 16 nnz per row, 16 384 samples; 0.98 MB of fp64 structure):
+  // fp64 1 585 -> 1 384 ms per launch (S = 2), fp32 952 -> 750 ms (S = 4);
+  // configurations 1 and 2 (0.12 and 0.25 MB) are faster on the narrow tiles
+  // (configuration 2: 125.2 ms against 129.7 with S = 2 and 171.6 with S = 4).
+  // Taken above 384 KB of structure when the batch fills one tile per SM.
+  const size_t structure_bytes =
+      (size_t)(plan->sell[0].nnz_r + (size_t)plan->sell[0].nnz_c) * (w + sizeof(uint16_t));
+  if (!qp && best >= 0 && forced == 0 && forced_threads == 0 && structure_bytes > (384u << 10)) {
+    for (const int S : {4, 2}) {
+      int k = kFirstWideShape;
+      while (k < kForwardShapeCount && !(kShapes[k][0] == S && kShapes[k][1] == 768)) ++k;
+      const size_t stat = f64 ? purin::forward_static_smem<double>(S, 768)
+                              : purin::forward_static_smem<float>(S, 768);
+      if (k == kForwardShapeCount || (size_t)S * per_sample + stat + 1024 > cap ||
+          batch < (int64_t)S * sms)
+        continue;
+      int& cached = plan->fwd_blocks[pv ? 1 : 0][shared_values ? 1 : 0][k];
+      if (cached < 0) {
+        const size_t dyn = (size_t)S * per_sample;
+        cached = f64 ? purin::forward_blocks_per_sm<double>(S, 768, shared_values, dyn, false)
+                     : purin::forward_blocks_per_sm<float>(S, 768, shared_values, dyn, false);
+      }
+      if (cached >= 1) {
+        best = k;
+        break;
+      }
+    }
+  }
   if (best >= 0) {
     fp.S = kShapes[best][0];
     fp.NT = kShapes[best][1];

@@ -243,10 +243,17 @@ __device__ __forceinline__ T dual_minimiser(T tt, T qj, T l, T u) {
 }
 
 // Resident CTAs per SM the register budget is sized for (64 registers per
-// thread for one-sample tiles): 1 x 1024, 2 x 512, 8 x 128, or 4 / 2 / 1 CTAs
-// of 256 threads for S = 1 / 2 / wider.
+// thread for one-sample tiles): 1 x 1024 or 768, 2 x 512 (one CTA of 512 for
+// wider tiles, 128 registers), 8 x 128, or 4 / 2 / 1 CTAs of 256 threads for
+// S = 1 / 2 / wider.
+// Wide multi-sample shared-memory tiles (S, NT): one CTA per SM, registers
+// 65536 / NT (128 for 512 threads, 80 for 768, 64 for 1024).
+#define PURIN_WIDE_TILES                                                                   \
+  PURIN_WIDE_TILE(2, 512) PURIN_WIDE_TILE(4, 512) PURIN_WIDE_TILE(2, 768) PURIN_WIDE_TILE(4, 768) \
+  PURIN_WIDE_TILE(2, 1024) PURIN_WIDE_TILE(4, 1024)
+
 constexpr int forward_min_blocks(int S, int NT) {
-  return NT >= 1024 ? 1 : NT >= 512 ? 2 : NT <= 128 ? 8 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
+  return NT >= 1024 ? 1 : NT >= 512 ? (S == 1 ? 2 : 1) : NT <= 128 ? 8 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
 }
 
 template <typename T, int S, int NT, bool kSmem, bool kShared, bool kQP>
@@ -970,8 +977,10 @@ cudaError_t launch_s(const FwdParams<T>& p, bool smem, size_t smem_bytes, cudaSt
   return cudaGetLastError();
 }
 
-// Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads, and S = 1
-// with 2 or 4 times as many threads for shared-memory tiles of one sample.
+// Instantiated shapes: S = 1, 2, 4, 8 with kForwardThreads threads; S = 1 with
+// 2 or 4 times as many; and the wide multi-sample tiles of PURIN_WIDE_TILES
+// (not built for the QP), for samples so large that one tile fills an SM: its
+// samples share every structure load, and its threads keep the SM's warps.
 // The diagonal QP is built for the one-sample shapes only, plus one-sample
 // tiles of kNarrowThreads threads.
 template <typename T, bool kShared, bool kQP>
@@ -983,12 +992,15 @@ cudaError_t launch_shared(const FwdParams<T>& p, int S, int NT, bool smem, size_
                                                                             stream)
                             : cudaErrorInvalidValue;
   }
-  if (NT == 2 * kForwardThreads)
-    return S == 1 ? launch_s<T, 1, 2 * kForwardThreads, kShared, kQP>(p, smem, smem_bytes, stream)
-                  : cudaErrorInvalidValue;
-  if (NT == kWideThreads)
-    return S == 1 ? launch_s<T, 1, kWideThreads, kShared, kQP>(p, smem, smem_bytes, stream)
-                  : cudaErrorInvalidValue;
+  if (S == 1 && NT == 2 * kForwardThreads)
+    return launch_s<T, 1, 2 * kForwardThreads, kShared, kQP>(p, smem, smem_bytes, stream);
+  if (S == 1 && NT == kWideThreads) return launch_s<T, 1, kWideThreads, kShared, kQP>(p, smem, smem_bytes, stream);
+  if constexpr (!kQP) {
+#define PURIN_WIDE_TILE(SS, NN) \
+  if (S == SS && NT == NN) return launch_s<T, SS, NN, kShared, false>(p, smem, smem_bytes, stream);
+    PURIN_WIDE_TILES
+#undef PURIN_WIDE_TILE
+  }
   if (NT != kForwardThreads) return cudaErrorInvalidValue;
   if constexpr (kQP) {
     return S == 1 ? launch_s<T, 1, kForwardThreads, kShared, true>(p, smem, smem_bytes, stream)
@@ -1022,10 +1034,15 @@ int blocks_per_sm_shared(int S, int NT, size_t smem_bytes) {
     if (NT == kNarrowThreads)
       return S == 1 ? blocks_per_sm_s<T, 1, kNarrowThreads, kShared, true>(smem_bytes) : 0;
   }
-  if (NT == 2 * kForwardThreads)
-    return S == 1 ? blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared, kQP>(smem_bytes) : 0;
-  if (NT == kWideThreads)
-    return S == 1 ? blocks_per_sm_s<T, 1, kWideThreads, kShared, kQP>(smem_bytes) : 0;
+  if (S == 1 && NT == 2 * kForwardThreads)
+    return blocks_per_sm_s<T, 1, 2 * kForwardThreads, kShared, kQP>(smem_bytes);
+  if (S == 1 && NT == kWideThreads) return blocks_per_sm_s<T, 1, kWideThreads, kShared, kQP>(smem_bytes);
+  if constexpr (!kQP) {
+#define PURIN_WIDE_TILE(SS, NN) \
+  if (S == SS && NT == NN) return blocks_per_sm_s<T, SS, NN, kShared, false>(smem_bytes);
+    PURIN_WIDE_TILES
+#undef PURIN_WIDE_TILE
+  }
   if (NT != kForwardThreads) return 0;
   if constexpr (kQP) {
     return S == 1 ? blocks_per_sm_s<T, 1, kForwardThreads, kShared, true>(smem_bytes) : 0;
@@ -1096,8 +1113,12 @@ int forward_blocks_per_sm(int S, int NT, bool shared_values, size_t smem_bytes, 
 template <typename T>
 size_t forward_static_smem(int S, int NT) {
   if (NT == kNarrowThreads) return sizeof(TileScratch<T, 1, kNarrowThreads / 32>);
-  if (NT == 2 * kForwardThreads) return sizeof(TileScratch<T, 1, 2 * kForwardThreads / 32>);
-  if (NT == kWideThreads) return sizeof(TileScratch<T, 1, kWideThreads / 32>);
+  if (S == 1 && NT == 2 * kForwardThreads) return sizeof(TileScratch<T, 1, 2 * kForwardThreads / 32>);
+  if (S == 1 && NT == kWideThreads) return sizeof(TileScratch<T, 1, kWideThreads / 32>);
+#define PURIN_WIDE_TILE(SS, NN) \
+  if (S == SS && NT == NN) return sizeof(TileScratch<T, SS, NN / 32>);
+  PURIN_WIDE_TILES
+#undef PURIN_WIDE_TILE
   switch (S) {
     case 1: return sizeof(TileScratch<T, 1, kForwardThreads / 32>);
     case 2: return sizeof(TileScratch<T, 2, kForwardThreads / 32>);

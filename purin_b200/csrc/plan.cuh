@@ -50,6 +50,9 @@ struct DevStructure {
 
 }  // namespace purin
 
+// Forward tile shapes the planner considers (capi.cu's shape table).
+constexpr int kForwardShapeCount = 13;
+
 struct PurinCpPlan {
   PurinCpPlanInfo info;
   purin::DevStructure dev;
@@ -66,8 +69,11 @@ struct PurinCpPlan {
   // (-1: not queried yet); filled on first use, the same value by any thread.
   // [distance | distance + diagonal steps | QP | QP with per-variable coefficients]
   // x [per-sample values | shared values] x tile shape
-  int fwd_blocks[4][2][8] = {{{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
-                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
-                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}},
-                             {{-1, -1, -1, -1, -1, -1, -1, -1}, {-1, -1, -1, -1, -1, -1, -1, -1}}};
+  int fwd_blocks[4][2][kForwardShapeCount];
+
+  PurinCpPlan() {
+    for (auto& a : fwd_blocks)
+      for (auto& b : a)
+        for (int& c : b) c = -1;
+  }
 };

@@ -120,7 +120,8 @@ _TILE_ORACLE = {}
 
 
 @pytest.mark.parametrize("samples_per_tile,threads", [(1, 256), (2, 256), (4, 256), (8, 256),
-                                                     (1, 512), (1, 1024)])
+                                                     (1, 512), (1, 1024), (2, 512), (4, 512),
+                                                     (2, 768), (4, 768), (2, 1024), (4, 1024)])
 @pytest.mark.parametrize("name,dtype,overrides", TILE_CASES, ids=[c[0] for c in TILE_CASES])
 def test_forward_tile_widths_match_oracle(monkeypatch, samples_per_tile, threads, name, dtype,
                                           overrides):
