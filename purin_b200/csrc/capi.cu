@@ -47,6 +47,7 @@ struct DeviceGuard {
 };
 
 size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
+int round_up_int(int x, int to) { return (x + to - 1) / to * to; }
 
 size_t dtype_size(int32_t dtype) { return dtype == PURIN_FLOAT64 ? 8 : 4; }
 
@@ -193,9 +194,8 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   // configurations 1 and 2 (0.12 and 0.25 MB) are faster on the narrow tiles
   // (configuration 2: 125.2 ms against 129.7 with S = 2 and 171.6 with S = 4).
   // Taken above 384 KB of structure when the batch fills one tile per SM.
-  const size_t structure_bytes =
-      (size_t)(plan->sell[0].nnz_r + (size_t)plan->sell[0].nnz_c) * (w + sizeof(uint16_t));
-  if (!qp && best >= 0 && forced == 0 && forced_threads == 0 && structure_bytes > (384u << 10)) {
+  if (!qp && best >= 0 && forced == 0 && forced_threads == 0 &&
+      wide_structure(plan->info.kept_nnz, w)) {
     for (const int S : {4, 2}) {
       int k = kFirstWideShape;
       while (k < kForwardShapeCount && !(kShapes[k][0] == S && kShapes[k][1] == 768)) ++k;
@@ -1048,8 +1048,16 @@ int32_t create_plan(const PurinCpStructure* s, PurinCpPlan** out, bool presolve_
       int64_t moves = std::min<int64_t>(200 * lines, 1000000);
       // PURIN_CP_BANK_MOVES overrides the search budget (for comparisons).
       if (const char* env = std::getenv("PURIN_CP_BANK_MOVES")) moves = std::atoll(env);
-      purin::bank_aware_orders(info.kept_rows, n, krow_ptr, kcol, kcol_ptr, kcsc_row,
-                               (int)dtype_size(info.dtype), moves, rorder, corder);
+      // Order for the wide tiles' gathers when the forward will take them: a
+      // large structure and room for two samples' state (y, ybar, duals,
+      // padded to whole slices) in one CTA's shared memory.
+      const size_t w = dtype_size(info.dtype);
+      const size_t pair_state =
+          2 * (size_t)(2 * (round_up_int(n, 32) + 1) + round_up_int(info.kept_rows, 32) + 1) * w;
+      const bool wide = wide_structure(info.kept_nnz, w) &&
+                        pair_state + (16u << 10) <= (size_t)plan->max_smem_optin;
+      purin::bank_aware_orders(info.kept_rows, n, krow_ptr, kcol, kcol_ptr, kcsc_row, (int)w, wide,
+                               moves, rorder, corder);
     }
     SellHost rows_h = build_sell(info.kept_rows, krow_ptr, kcol, nullptr, C, n, rorder);
     SellHost cols_h = build_sell(n, kcol_ptr, kcsc_row, &kcsc_slot, C, info.kept_rows, corder);

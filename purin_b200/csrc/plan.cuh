@@ -53,6 +53,14 @@ struct DevStructure {
 // Forward tile shapes the planner considers (capi.cu's shape table).
 constexpr int kForwardShapeCount = 13;
 
+// A structure whose stored entries (value plus 16-bit index, both products)
+// exceed 384 KB streams from L2 once per tile-iteration; the forward then uses
+// wide multi-sample tiles (16-byte gathers per lane), and the bank-aware line
+// order is chosen for those gathers.
+inline bool wide_structure(int64_t kept_nnz, size_t elem_bytes) {
+  return (size_t)(2 * kept_nnz) * (elem_bytes + sizeof(uint16_t)) > (384u << 10);
+}
+
 struct PurinCpPlan {
   PurinCpPlanInfo info;
   purin::DevStructure dev;

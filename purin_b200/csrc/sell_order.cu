@@ -52,7 +52,8 @@ struct Change {
 
 BankOrderStats bank_aware_orders(int m, int n, const std::vector<int32_t>& r_ptr,
                                  const std::vector<int32_t>& r_col, const std::vector<int32_t>& c_ptr,
-                                 const std::vector<int32_t>& c_row, int elem_bytes, int64_t max_moves,
+                                 const std::vector<int32_t>& c_row, int elem_bytes, bool wide_tiles,
+                                 int64_t max_moves,
                                  std::vector<int>& row_order, std::vector<int>& col_order) {
   BankOrderStats stats;
   if (m <= 0 || n <= 0) return stats;
@@ -96,9 +97,11 @@ BankOrderStats bank_aware_orders(int m, int n, const std::vector<int32_t>& r_ptr
   for (int p = 0; p < m; ++p) rpos[row_order[p]] = p;
   for (int p = 0; p < n; ++p) cpos[col_order[p]] = p;
 
-  // Access levels: the tile widths S = 1 and S = 2 (element of S values per lane).
-  const int nl = 2;
-  const int level_group[2] = {elem_bytes == 8 ? 16 : 32, elem_bytes == 8 ? 8 : 16};
+  // Access levels: the tile widths S = 1 and S = 2 (element of S values per
+  // lane), or the 16-byte gathers of the wide tiles alone.
+  const int nl = wide_tiles ? 1 : 2;
+  int level_group[2] = {elem_bytes == 8 ? 16 : 32, elem_bytes == 8 ? 8 : 16};
+  if (wide_tiles) level_group[0] = 8;
   std::vector<Table> rowt(nl), colt(nl);  // row pass (gathers y), column pass (gathers lambda)
   for (int l = 0; l < nl; ++l) {
     rowt[l].init(m, rsteps, level_group[l], level_group[l]);

@@ -33,10 +33,14 @@ struct BankOrderStats {
 // line and are sorted by line length, descending; on return each is permuted
 // within its runs of equal length.  Rows are given in CSR (r_ptr, r_col), columns
 // in CSC (c_ptr, c_row) with entries in the order the kernel accumulates them.
-// elem_bytes is the iterate's element size (4 or 8); max_moves caps the search.
+// elem_bytes is the iterate's element size (4 or 8); the search minimises the
+// passes of the one- and two-sample tiles' gathers, or with wide_tiles only those
+// of the 16-byte gathers of the wide multi-sample tiles (quarter-warps, position
+// mod 8).  max_moves caps the search.
 BankOrderStats bank_aware_orders(int m, int n, const std::vector<int32_t>& r_ptr,
                                  const std::vector<int32_t>& r_col, const std::vector<int32_t>& c_ptr,
-                                 const std::vector<int32_t>& c_row, int elem_bytes, int64_t max_moves,
-                                 std::vector<int>& row_order, std::vector<int>& col_order);
+                                 const std::vector<int32_t>& c_row, int elem_bytes, bool wide_tiles,
+                                 int64_t max_moves, std::vector<int>& row_order,
+                                 std::vector<int>& col_order);
 
 }  // namespace purin
