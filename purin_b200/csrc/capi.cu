@@ -190,10 +190,12 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   // products).  A wide tile of 4 (else 2) samples on 768 threads shares that
   // stream among its samples and keeps 24 warps.  Configuration 4 (n = 4096,
   // m = 3072, 16 nnz per row, 16 384 samples; 0.98 MB of fp64 structure):
-  // fp64 1 585 -> 1 384 ms per launch (S = 2), fp32 952 -> 750 ms (S = 4);
+  // fp64 1 585 -> 1 384 ms per launch (S = 2), fp32 952 -> 750 ms (S = 4),
+  // and 1 360 / 696 ms with the line order chosen for these tiles' gathers;
   // configurations 1 and 2 (0.12 and 0.25 MB) are faster on the narrow tiles
   // (configuration 2: 125.2 ms against 129.7 with S = 2 and 171.6 with S = 4).
   // Taken above 384 KB of structure when the batch fills one tile per SM.
+  // Every tile shape gives the same bits, so shards may differ in shape.
   if (!qp && best >= 0 && forced == 0 && forced_threads == 0 &&
       wide_structure(plan->info.kept_nnz, w)) {
     for (const int S : {4, 2}) {
