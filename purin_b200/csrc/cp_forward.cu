@@ -242,22 +242,29 @@ __device__ __forceinline__ T dual_minimiser(T tt, T qj, T l, T u) {
   }
 }
 
-// Resident CTAs per SM the register budget is sized for (64 registers per
-// thread for one-sample tiles): 1 x 1024 or 768, 2 x 512 (one CTA of 512 for
-// wider tiles, 128 registers), 8 x 128, or 4 / 2 / 1 CTAs of 256 threads for
-// S = 1 / 2 / wider.
 // Wide multi-sample shared-memory tiles (S, NT): one CTA per SM, registers
 // 65536 / NT (128 for 512 threads, 80 for 768, 64 for 1024).
 #define PURIN_WIDE_TILES                                                                   \
   PURIN_WIDE_TILE(2, 512) PURIN_WIDE_TILE(4, 512) PURIN_WIDE_TILE(2, 768) PURIN_WIDE_TILE(4, 768) \
   PURIN_WIDE_TILE(2, 1024) PURIN_WIDE_TILE(4, 1024)
 
-constexpr int forward_min_blocks(int S, int NT) {
-  return NT >= 1024 ? 1 : NT >= 512 ? (S == 1 ? 2 : 1) : NT <= 128 ? 8 : (S == 1) ? 4 : (S <= 2) ? 2 : 1;
+// Resident CTAs per SM the register budget is sized for (64 registers per
+// thread for one-sample tiles): 1 x 1024 or 768, 2 x 512 (one CTA of 512 for
+// wider tiles, 128 registers), 8 x 128, or 4 / 2 / 1 CTAs of 256 threads for
+// S = 1 / 2 / wider.  fp32 two-sample tiles also fit 64 registers (no spills;
+// 87 unconstrained), so they keep 4 CTAs per SM like the one-sample tiles.
+constexpr int forward_min_blocks(int S, int NT, int elem_bytes) {
+  return NT >= 1024                    ? 1
+         : NT >= 512                   ? (S == 1 ? 2 : 1)
+         : NT <= 128                   ? 8
+         : S == 1                      ? 4
+         : (S == 2 && elem_bytes == 4) ? 4
+         : S == 2                      ? 2
+                                       : 1;
 }
 
 template <typename T, int S, int NT, bool kSmem, bool kShared, bool kQP>
-__global__ void __launch_bounds__(NT, forward_min_blocks(S, NT))
+__global__ void __launch_bounds__(NT, forward_min_blocks(S, NT, (int)sizeof(T)))
 cp_forward_kernel(const FwdParams<T> p) {
   constexpr int kThreads = NT;
   constexpr int kWarps = NT / 32;
