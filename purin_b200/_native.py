@@ -134,7 +134,8 @@ class AdmmAdjointArgs(ctypes.Structure):
 EXPORTED = (
     "purin_cp_abi_version", "purin_cp_last_error", "purin_cp_plan_create",
     "purin_cp_plan_destroy", "purin_cp_plan_info", "purin_cp_plan_indices",
-    "purin_cp_workspace_size", "purin_cp_forward", "purin_cp_adjoint", "purin_cp_adjoint_stage",
+    "purin_cp_workspace_size", "purin_cp_forward_shape", "purin_cp_forward", "purin_cp_adjoint",
+    "purin_cp_adjoint_stage",
     "purin_cp_postprocess", "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
     "purin_qp_adjoint_stage", "purin_admm_workspace_size", "purin_admm_forward",
     "purin_admm_adjoint_workspace_size", "purin_admm_adjoint", "purin_admm_adjoint_stage",
@@ -169,6 +170,8 @@ def load():
     lib.purin_cp_workspace_size.argtypes = [c_vp, c_i32, c_i64, ctypes.POINTER(CpConfig),
                                             ctypes.POINTER(LinearConfig),
                                             ctypes.POINTER(ctypes.c_size_t)]
+    lib.purin_cp_forward_shape.argtypes = [c_vp, ctypes.POINTER(CpConfig), c_i64, c_i32, c_i32p,
+                                           c_i32p, c_i32p]
     lib.purin_cp_forward.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(ForwardArgs),
                                      c_vp, ctypes.c_size_t, c_vp]
     lib.purin_cp_adjoint.argtypes = [c_vp, ctypes.POINTER(CpConfig), ctypes.POINTER(LinearConfig),
@@ -202,7 +205,8 @@ def load():
                  "purin_admm_adjoint_stage"):
         getattr(lib, name).restype = c_i32
     for name in ("purin_cp_plan_create", "purin_cp_plan_destroy", "purin_cp_plan_info",
-                 "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward",
+                 "purin_cp_plan_indices", "purin_cp_workspace_size", "purin_cp_forward_shape",
+                 "purin_cp_forward",
                  "purin_cp_adjoint", "purin_cp_adjoint_stage", "purin_cp_postprocess",
                  "purin_qp_plan_create", "purin_qp_forward", "purin_qp_adjoint",
                  "purin_qp_adjoint_stage"):
@@ -260,6 +264,15 @@ class Plan:
             ctypes.byref(lin) if lin is not None else None, ctypes.byref(size)),
             "purin_cp_workspace_size")
         return int(size.value)
+
+    def forward_shape(self, cfg: CpConfig, batch: int, shared_values: bool = True):
+        """(samples per tile, threads per CTA, tile state in shared memory) of a forward call."""
+        out = [ctypes.c_int32() for _ in range(3)]
+        check(self._lib.purin_cp_forward_shape(self.handle, ctypes.byref(cfg), int(batch),
+                                               int(bool(shared_values)),
+                                               *[ctypes.byref(o) for o in out]),
+              "purin_cp_forward_shape")
+        return out[0].value, out[1].value, bool(out[2].value)
 
     def forward(self, cfg, args, workspace_ptr, workspace_bytes, stream):
         check(self._lib.purin_cp_forward(self.handle, ctypes.byref(cfg), ctypes.byref(args),

@@ -1219,6 +1219,23 @@ int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t bat
   return fail(PURIN_ERR_INVALID_ARGUMENT, "unknown op");
 }
 
+int32_t purin_cp_forward_shape(const PurinCpPlan* plan, const PurinCpConfig* config, int64_t batch,
+                               int32_t shared_values, int32_t* samples_per_tile, int32_t* threads,
+                               int32_t* shared_state) {
+  if (int32_t r = check_plan(plan)) return r;
+  if (int32_t r = check_config(config)) return r;
+  if (!samples_per_tile || !threads || !shared_state)
+    return fail(PURIN_ERR_INVALID_ARGUMENT, "an output pointer is NULL");
+  if (batch < 1) return fail(PURIN_ERR_INVALID_ARGUMENT, "batch must be positive");
+  DeviceGuard guard(plan->info.device);
+  // As purin_cp_forward plans it: a single sample counts as shared values.
+  const FwdPlan fp = plan_forward(plan, config, batch, shared_values != 0 || batch == 1);
+  *samples_per_tile = fp.S;
+  *threads = fp.NT;
+  *shared_state = fp.smem ? 1 : 0;
+  return PURIN_OK;
+}
+
 int32_t purin_cp_forward(const PurinCpPlan* plan, const PurinCpConfig* config, const PurinCpForwardArgs* args,
                          void* workspace, size_t workspace_bytes, void* stream) {
   if (int32_t r = check_plan(plan)) return r;

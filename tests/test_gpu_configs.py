@@ -80,6 +80,29 @@ def test_config4_weighted_distance(dtype):
     _assert_forward(got, expected, residual_factor=factor)
 
 
+@pytest.mark.parametrize("dtype,samples", [(np.float64, 2), (np.float32, 4)])
+def test_config4_wide_tiles_equal_one_sample_tiles(monkeypatch, dtype, samples):
+    """Config 4's structure (0.98 MB in fp64) takes the wide tiles once the batch fills
+    one per SM: 2 (fp64) or 4 (fp32) samples on 768 threads, lines ordered for their
+    16-byte gathers.  The whole public solve then equals the one-sample tiles' bit for bit
+    (every tile shape gives the oracle's bits: test_forward_tile_widths_match_oracle)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    batch = samples * sms
+    w = make_workload(4, batch)
+    cfg = replace(w.config, max_iterations=60,
+                  metric_diagonal=tuple(float(v) for v in w.weights))
+    layer = _layer(w.problem, cfg, batch, dtype)
+    assert layer._plan.forward_shape(layer._cfg, batch) == (samples, 768, True)
+    wide = layer.solve(_t(w.candidates, dtype), _t(w.theta, dtype))
+    monkeypatch.setenv("PURIN_CP_SAMPLES_PER_TILE", "1")
+    monkeypatch.setenv("PURIN_CP_TILE_THREADS", "256")
+    assert layer._plan.forward_shape(layer._cfg, batch) == (1, 256, True)
+    narrow = layer.solve(_t(w.candidates, dtype), _t(w.theta, dtype))
+    for field in FIELDS + ("residual_inf_norm",):
+        np.testing.assert_array_equal(getattr(wide, field).cpu().numpy(),
+                                      getattr(narrow, field).cpu().numpy(), err_msg=field)
+
+
 def test_config2_forward_and_candidate_gradient():
     """fp64, n = 2048, loss 0.5 ||y - t||^2 with samples that converge (CP tolerance 1e-3)."""
     batch = 2
