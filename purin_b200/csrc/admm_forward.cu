@@ -30,8 +30,12 @@ namespace purin {
 
 namespace {
 
+// Threads per sample: one warp for small problems (every vector at most
+// kAdmmWarpEntries long), whose reductions are shuffles behind a one-warp
+// barrier and whose samples all fit on the GPU at once; 256 otherwise.
 constexpr int kAdmmThreads = 256;
-constexpr int kAdmmWarps = kAdmmThreads / 32;
+constexpr int kAdmmWarpEntries = 256;
+constexpr size_t kAdmmStageBytes = 24u << 10;
 
 // Block reduction of up to three values: sums of a and b, max of c.  Every
 // thread receives the results.
@@ -40,7 +44,7 @@ struct Red3 {
   T a, b, c;
 };
 
-template <typename T>
+template <int kWarps, typename T>
 __device__ Red3<T> block_reduce3(T a, T b, T c, T (*scratch)[3]) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -57,7 +61,7 @@ __device__ Red3<T> block_reduce3(T a, T b, T c, T (*scratch)[3]) {
   __syncthreads();
   Red3<T> r{T(0), T(0), T(0)};
 #pragma unroll
-  for (int w = 0; w < kAdmmWarps; ++w) {
+  for (int w = 0; w < kWarps; ++w) {
     r.a = r.a + scratch[w][0];
     r.b = r.b + scratch[w][1];
     r.c = pmax(r.c, scratch[w][2]);
@@ -66,21 +70,27 @@ __device__ Red3<T> block_reduce3(T a, T b, T c, T (*scratch)[3]) {
   return r;
 }
 
+// One sample's operands.  The structure, values and per-sample vectors are read
+// through these pointers: global memory, or copies in shared memory (staged).
 template <typename T>
 struct AdmmSample {
-  const DevStructure* st;
+  const int* row_ptr;   // m + 1
+  const int* col;       // nnz
+  const int* col_ptr;   // n + 1
+  const int* csc_row;   // nnz
+  const int* csc_slot;  // nnz
   const T* vals;
   const T* q;
   const T* c;
   const T* lo;
   const T* up;
-  int n, m;
+  int n, m, nnz;
 
   // out[i] = (K v)_i for rows i (CSR order).
   __device__ void mv(const T* v, T* out) const {
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
       T acc = T(0);
-      for (int k = st->row_ptr[i]; k < st->row_ptr[i + 1]; ++k) acc = acc + vals[k] * v[st->col[k]];
+      for (int k = row_ptr[i]; k < row_ptr[i + 1]; ++k) acc = acc + vals[k] * v[col[k]];
       out[i] = acc;
     }
     __syncthreads();
@@ -89,15 +99,69 @@ struct AdmmSample {
   __device__ void tmv(const T* w, T* out, bool square = false) const {
     for (int j = threadIdx.x; j < n; j += blockDim.x) {
       T acc = T(0);
-      for (int e = st->col_ptr[j]; e < st->col_ptr[j + 1]; ++e) {
-        const T v = vals[st->csc_slot[e]];
-        acc = acc + (square ? v * v : v) * w[st->csc_row[e]];
+      for (int e = col_ptr[j]; e < col_ptr[j + 1]; ++e) {
+        const T v = vals[csc_slot[e]];
+        acc = acc + (square ? v * v : v) * w[csc_row[e]];
       }
       out[j] = acc;
     }
     __syncthreads();
   }
 };
+
+// Elements of the staged copies: T values (vals, q, c, lo, up), then ints.
+__host__ __device__ inline size_t admm_stage_values(int n, int m, int nnz) {
+  return (size_t)nnz + 2 * (size_t)n + 2 * (size_t)m;
+}
+__host__ __device__ inline size_t admm_stage_ints(int n, int m, int nnz) {
+  return (size_t)(m + 1) + (size_t)(n + 1) + 3 * (size_t)nnz;
+}
+
+// Copy the sample's operands into shared memory at `at` (after the state
+// vectors) and point S at the copies: every product then gathers from shared
+// memory instead of making dependent L2 round trips.
+template <typename T>
+__device__ void stage_sample(AdmmSample<T>& S, T* at) {
+  const int n = S.n, m = S.m, nnz = S.nnz;
+  T* vals = at;
+  T* q = vals + nnz;
+  T* c = q + n;
+  T* lo = c + n;
+  T* up = lo + m;
+  int* ints = reinterpret_cast<int*>(up + m);
+  int* row_ptr = ints;
+  int* col = row_ptr + m + 1;
+  int* col_ptr = col + nnz;
+  int* csc_row = col_ptr + n + 1;
+  int* csc_slot = csc_row + nnz;
+  for (int k = threadIdx.x; k < nnz; k += blockDim.x) {
+    vals[k] = S.vals[k];
+    col[k] = S.col[k];
+    csc_row[k] = S.csc_row[k];
+    csc_slot[k] = S.csc_slot[k];
+  }
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    q[j] = S.q[j];
+    c[j] = S.c[j];
+  }
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    lo[i] = S.lo[i];
+    up[i] = S.up[i];
+  }
+  for (int i = threadIdx.x; i <= m; i += blockDim.x) row_ptr[i] = S.row_ptr[i];
+  for (int j = threadIdx.x; j <= n; j += blockDim.x) col_ptr[j] = S.col_ptr[j];
+  __syncthreads();
+  S.vals = vals;
+  S.q = q;
+  S.c = c;
+  S.lo = lo;
+  S.up = up;
+  S.row_ptr = row_ptr;
+  S.col = col;
+  S.col_ptr = col_ptr;
+  S.csc_row = csc_row;
+  S.csc_slot = csc_slot;
+}
 
 // Vectors of one CTA: 9 of length n, 5 of length m.
 template <typename T>
@@ -188,16 +252,22 @@ __device__ void band_solve(const AdmmParams<T>& p, int n, const T* band, const T
   __syncthreads();
 }
 
-template <typename T, bool kSmem>
-__global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmParams<T> p) {
+template <typename T, bool kSmem, int NT, bool kStage>
+__global__ void __launch_bounds__(NT) admm_forward_kernel(const AdmmParams<T> p) {
+  constexpr int kWarps = NT / 32;
   extern __shared__ __align__(16) unsigned char dyn[];
-  __shared__ T red[kAdmmWarps][3];
+  __shared__ T red[kWarps][3];
   const int64_t X = blockIdx.x;
   if (X >= p.batch) return;
   const DevStructure& st = p.st;
   const int n = st.n, m = st.m;
   AdmmSample<T> S;
-  S.st = &st;
+  S.row_ptr = st.row_ptr;
+  S.col = st.col;
+  S.col_ptr = st.col_ptr;
+  S.csc_row = st.csc_row;
+  S.csc_slot = st.csc_slot;
+  S.nnz = st.nnz;
   S.vals = p.values + X * p.values_stride;
   S.q = p.q + X * n;
   S.c = p.c + X * n;
@@ -208,6 +278,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
   const size_t elems = 9 * (size_t)n + 5 * (size_t)m;
   T* base = kSmem ? reinterpret_cast<T*>(dyn) : p.gstate + X * elems;
   const AdmmState<T> V = carve(base, n, m);
+  if constexpr (kStage) stage_sample(S, reinterpret_cast<T*>(dyn) + elems);
   const T zero = T(0), one = T(1);
   const T sigma = p.sigma, alpha = p.alpha;
   const T tol = p.tolerance[X];
@@ -255,7 +326,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
           V.r[j] = corr;
           cmax = pmax(cmax, fabs(corr));
         }
-        const T magnitude = pmax(block_reduce3(zero, zero, cmax, red).c, tiny);
+        const T magnitude = pmax(block_reduce3<kWarps>(zero, zero, cmax, red).c, tiny);
         // PCG from zero (fischer_burmeister/solver.py:213-310): the residual of the
         // zero start is b itself (op(0) is an exact zero).
         T rz_part = zero, rmax0 = zero;
@@ -271,7 +342,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
           rmax0 = pmax(rmax0, fabs(rj));
           bad |= (finite(rj) && finite(zj)) ? 0 : 1;
         }
-        const Red3<T> r0 = block_reduce3(rz_part, T(bad), rmax0, red);
+        const Red3<T> r0 = block_reduce3<kWarps>(rz_part, T(bad), rmax0, red);
         T rz = r0.a;
         const T threshold = pmax(p.cg_tolerance, p.cg_tolerance * r0.c);
         bool active = r0.b == zero && finite(rz) && r0.c > threshold;
@@ -280,7 +351,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
           admm_op(S, V, sigma, V.d, V.img);
           T cpart = zero;
           for (int j = threadIdx.x; j < n; j += blockDim.x) cpart = cpart + V.d[j] * V.img[j];
-          const T curvature = block_reduce3(cpart, zero, zero, red).a;
+          const T curvature = block_reduce3<kWarps>(cpart, zero, zero, red).a;
           const bool positive = curvature > eps;
           const T step_len = rz / (positive ? curvature : one);
           T nrz = zero, rmax = zero;
@@ -296,7 +367,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
             rmax = pmax(rmax, fabs(rj));
             nbad |= (finite(xs) && finite(rj) && finite(zj)) ? 0 : 1;
           }
-          const Red3<T> rr = block_reduce3(nrz, T(nbad), rmax, red);
+          const Red3<T> rr = block_reduce3<kWarps>(nrz, T(nbad), rmax, red);
           const T beta = rr.a / (fabs(rz) > eps ? rz : one);
           for (int j = threadIdx.x; j < n; j += blockDim.x) V.d[j] = V.zc[j] + beta * V.d[j];
           __syncthreads();
@@ -323,7 +394,7 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
       T lmax = zero;
       for (int j = threadIdx.x; j < n; j += blockDim.x)
         lmax = pmax(lmax, fabs(V.rhs[j] - ((S.q[j] + sigma) * V.xt[j] + V.img[j])));
-      linear = block_reduce3(zero, zero, lmax, red).c;
+      linear = block_reduce3<kWarps>(zero, zero, lmax, red).c;
     }
     for (int j = threadIdx.x; j < n; j += blockDim.x) V.x[j] = alpha * V.xt[j] + (one - alpha) * V.x[j];
     for (int i = threadIdx.x; i < m; i += blockDim.x) {
@@ -349,8 +420,8 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
         dmax = pmax(dmax, fabs(S.q[j] * V.x[j] + S.c[j] + V.img[j]));
         bad |= finite(V.x[j]) ? 0 : 1;
       }
-      const Red3<T> a = block_reduce3(T(bad), zero, pmax_, red);
-      const Red3<T> b = block_reduce3(zero, zero, dmax, red);
+      const Red3<T> a = block_reduce3<kWarps>(T(bad), zero, pmax_, red);
+      const Red3<T> b = block_reduce3<kWarps>(zero, zero, dmax, red);
       primal = a.c;
       dual_res = b.c;
       fin = a.a == zero && finite(linear) && finite(primal) && finite(dual_res);
@@ -373,11 +444,11 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
         ky = pmax(ky, fabs(V.img[j]));
         cm = pmax(cm, fabs(S.c[j]));
       }
-      const T kxm = block_reduce3(zero, zero, kx, red).c;
-      const T zmm = block_reduce3(zero, zero, zm, red).c;
-      const T qxm = block_reduce3(zero, zero, qx, red).c;
-      const T kym = block_reduce3(zero, zero, ky, red).c;
-      const T cmm = block_reduce3(zero, zero, cm, red).c;
+      const T kxm = block_reduce3<kWarps>(zero, zero, kx, red).c;
+      const T zmm = block_reduce3<kWarps>(zero, zero, zm, red).c;
+      const T qxm = block_reduce3<kWarps>(zero, zero, qx, red).c;
+      const T kym = block_reduce3<kWarps>(zero, zero, ky, red).c;
+      const T cmm = block_reduce3<kWarps>(zero, zero, cm, red).c;
       const T pscale = pmax(pmax(kxm, zmm), T(1e-12));
       const T dscale = pmax(pmax(qxm, kym), pmax(cmm, T(1e-12)));
       const T rf = sqrt((primal / pscale + T(1e-16)) / (dual_res / dscale + T(1e-16)));
@@ -408,8 +479,8 @@ __global__ void __launch_bounds__(kAdmmThreads) admm_forward_kernel(const AdmmPa
     dmax = pmax(dmax, fabs(S.q[j] * V.x[j] + S.c[j] + V.img[j]));
     bad |= finite(V.x[j]) ? 0 : 1;
   }
-  const Red3<T> a = block_reduce3(T(bad), zero, pmax_, red);
-  const Red3<T> b = block_reduce3(zero, zero, dmax, red);
+  const Red3<T> a = block_reduce3<kWarps>(T(bad), zero, pmax_, red);
+  const Red3<T> b = block_reduce3<kWarps>(zero, zero, dmax, red);
   for (int j = threadIdx.x; j < n; j += blockDim.x) p.x[X * n + j] = V.x[j];
   for (int i = threadIdx.x; i < m; i += blockDim.x) {
     p.z[X * m + i] = V.z[i];
@@ -440,13 +511,26 @@ template <typename T>
 cudaError_t launch_admm(const AdmmParams<T>& p, bool smem, cudaStream_t stream) {
   if (p.batch <= 0) return cudaSuccess;
   const size_t bytes = admm_state_elems<T>(p.st.n, p.st.m) * sizeof(T);
-  if (smem) {
-    auto kern = admm_forward_kernel<T, true>;
+  const int n = p.st.n, m = p.st.m, nnz = p.st.nnz;
+  const bool warp = n <= kAdmmWarpEntries && m <= kAdmmWarpEntries;
+  // Small problems also stage their operands in shared memory when state and
+  // copies together stay within kAdmmStageBytes (about ten samples per SM).
+  const size_t staged = bytes + admm_stage_values(n, m, nnz) * sizeof(T) +
+                        admm_stage_ints(n, m, nnz) * sizeof(int);
+  if (smem && warp && staged <= kAdmmStageBytes) {
+    auto kern = admm_forward_kernel<T, true, 32, true>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)staged);
+    if (e != cudaSuccess) return e;
+    kern<<<(unsigned)p.batch, 32, staged, stream>>>(p);
+  } else if (smem) {
+    auto kern = warp ? admm_forward_kernel<T, true, 32, false> : admm_forward_kernel<T, true, kAdmmThreads, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
-    kern<<<(unsigned)p.batch, kAdmmThreads, bytes, stream>>>(p);
+    kern<<<(unsigned)p.batch, warp ? 32 : kAdmmThreads, bytes, stream>>>(p);
+  } else if (warp) {
+    admm_forward_kernel<T, false, 32, false><<<(unsigned)p.batch, 32, 0, stream>>>(p);
   } else {
-    admm_forward_kernel<T, false><<<(unsigned)p.batch, kAdmmThreads, 0, stream>>>(p);
+    admm_forward_kernel<T, false, kAdmmThreads, false><<<(unsigned)p.batch, kAdmmThreads, 0, stream>>>(p);
   }
   return cudaGetLastError();
 }

@@ -131,12 +131,15 @@ def _random_case(seed, n=40, me=6, mi=12, nnz=5, batch=5):
     return problem, theta, target
 
 
-@pytest.mark.parametrize("seed,adaptive,interval", [(1, False, 25), (2, True, 25), (3, False, 1)])
-def test_random_problems_match_the_oracle(seed, adaptive, interval):
+@pytest.mark.parametrize("seed,adaptive,interval,n", [(1, False, 25, 40), (2, True, 25, 40),
+                                                      (3, False, 1, 40), (4, False, 25, 300)])
+def test_random_problems_match_the_oracle(seed, adaptive, interval, n):
     """Random sparse problems with box rows (a row graph too wide for the band, so the
     PCG path; the boxes pair into two-sided rows): the projection, multipliers, iteration
-    counts and implicit gradients agree with the oracle."""
-    problem, theta, target = _random_case(seed)
+    counts and implicit gradients agree with the oracle.  n = 40 runs one-warp CTAs with
+    the operands staged in shared memory; n = 300 (more than 256 entries per vector) the
+    256-thread CTAs reading them from global memory."""
+    problem, theta, target = _random_case(seed, n=n)
     cfg = ADMMConfig(adaptive_rho=adaptive, check_interval=interval, implicit_gradient=
                      ImplicitGradientConfig(differentiate_problem_parameters=True),
                      linear_solver=LinearSolverConfig(tolerance=1e-11, max_iterations=300))
