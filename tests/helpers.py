@@ -181,3 +181,48 @@ class OracleADMMLayer:
 
     def __call__(self, target, theta=None):
         return self.solve(target, theta)[0]["y"]
+
+
+def coupled_diagonal_qp_case():
+    """tests/test_regression_cp_diagonal_steps.py:28-80 (seed 123): a diagonal QP with 2
+    equality and 8 coupled inequality rows on 6 variables in [-1, 1], 3 samples.
+    Returns (eq_rows, in_rows, (q, c, values, rhs, lower, upper), dense matrix)."""
+    rng = np.random.default_rng(123)
+    n, me, mi, batch = 6, 2, 8, 3
+    matrix = rng.normal(size=(me + mi, n))
+    matrix[abs(matrix) < 0.6] = 0
+    q = rng.uniform(0.5, 3.0, (batch, n))
+    c = rng.normal(size=(batch, n))
+    feasible = rng.uniform(-0.3, 0.3, (batch, n))
+    rhs = feasible @ matrix.T
+    rhs[:, me:] += rng.uniform(0.3, 1.0, (batch, mi))
+    rows = [tuple(int(j) for j in np.flatnonzero(r)) for r in matrix]
+    width = max(max(len(r) for r in rows), 1)
+    values = np.zeros((batch, me + mi, width))
+    for i, r in enumerate(rows):
+        values[:, i, :len(r)] = matrix[i, list(r)]
+    lower, upper = -np.ones((batch, n)), np.ones((batch, n))
+    return tuple(rows[:me]), tuple(rows[me:]), (q, c, values, rhs, lower, upper), matrix
+
+
+def kkt_certified_qp(q, c, matrix, rhs, me, lower, upper, y, tol=1e-6):
+    """The exact solution of min 0.5 y'diag(q)y + c'y s.t. A[:me] y = b[:me],
+    A[me:] y <= b[me:], lower <= y <= upper, on the active set that `y` (an approximate
+    solution) identifies: the KKT system of that set is solved exactly, and the result is
+    returned only if it is primal feasible and its multipliers have the right signs (a
+    certificate of optimality, standing in for the reference's OSQP comparison)."""
+    n = len(q)
+    ineq = [i for i in range(me, len(matrix)) if matrix[i] @ y >= rhs[i] - tol]
+    at_up = [j for j in range(n) if y[j] >= upper[j] - tol]
+    at_lo = [j for j in range(n) if y[j] <= lower[j] + tol]
+    A = np.vstack([matrix[:me], matrix[ineq], np.eye(n)[at_up], np.eye(n)[at_lo]])
+    b = np.r_[rhs[:me], rhs[ineq], upper[at_up], lower[at_lo]]
+    k = len(A)
+    kkt = np.block([[np.diag(q), A.T], [A, np.zeros((k, k))]])
+    sol = np.linalg.solve(kkt, np.r_[-c, b])
+    x, lam = sol[:n], sol[n:]
+    assert np.all(matrix[me:] @ x <= rhs[me:] + 1e-12), "active set not primal feasible"
+    assert np.all(x <= upper + 1e-12) and np.all(x >= lower - 1e-12)
+    signs = np.r_[np.zeros(me), np.ones(len(ineq) + len(at_up)), -np.ones(len(at_lo))]
+    assert np.all(lam[me:] * signs[me:] >= -1e-12), "multiplier signs"
+    return x

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import oracle_config
+from helpers import coupled_diagonal_qp_case, kkt_certified_qp, oracle_config
 from oracle.diagonal_qp import OracleDiagonalQP
 from purin_b200 import ChambollePockConfig, LinearSolverConfig
 from purin_b200.diagonal_qp import QPData, QPStructure, dense_qp_data
@@ -333,3 +333,22 @@ def test_gradients_fp32_match_oracle():
         scale = max(float(np.abs(g[name]).max()), 1e-6)
         np.testing.assert_allclose(t.grad.cpu().numpy(), g[name], rtol=0, atol=1e-4 * scale,
                                    err_msg=name)
+
+
+@pytest.mark.parametrize("diagonal", [False, True])
+def test_coupled_inequalities_match_a_certified_kkt_solution(diagonal):
+    """tests/test_regression_cp_diagonal_steps.py:28-80 on the QP kernels: converged
+    (tolerance 1e-9) to the exact solution within 3e-8 (an exact KKT solve on the
+    identified active set stands in for the reference's OSQP)."""
+    eq_rows, in_rows, data, matrix = coupled_diagonal_qp_case()
+    cfg = ChambollePockConfig(tolerance=1e-9, max_iterations=20000, row_scaling=False,
+                              diagonal_preconditioning=diagonal)
+    solver = QPStructure(6, eq_rows, in_rows).prepare(batch_size=3, config=cfg,
+                                                      dtype=torch.float64)
+    result = solver.solve(QPData(*(torch.as_tensor(a, device=DEV) for a in data)))
+    assert (result.status.cpu().numpy() == 0).all()
+    q, c, _, rhs, lower, upper = data
+    y = result.y.cpu().numpy()
+    for i in range(len(q)):
+        exact = kkt_certified_qp(q[i], c[i], matrix, rhs[i], 2, lower[i], upper[i], y[i])
+        np.testing.assert_allclose(y[i], exact, atol=3e-8)

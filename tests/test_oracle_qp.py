@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import oracle_config
+from helpers import coupled_diagonal_qp_case, kkt_certified_qp, oracle_config
 from oracle.cp import _balanced  # noqa: F401  (tie rule exercised by the pullback)
 from oracle.diagonal_qp import OracleDiagonalQP, qp_step_pullback
 from oracle.sparse import layout
@@ -147,3 +147,21 @@ def test_invalid_qp_structures():
 
     with pytest.raises(ValueError):
         dense_qp_data(np.ones(2), np.ones(2), np.empty((0, 2)), [], np.empty((0, 2)), [], -1, 1)
+
+
+@pytest.mark.parametrize("diagonal", [False, True])
+def test_coupled_inequalities_match_a_certified_kkt_solution(diagonal):
+    """tests/test_regression_cp_diagonal_steps.py:28-80: the general diagonal QP with
+    coupled inequalities converges (tolerance 1e-9) to the exact solution, within the
+    reference's 3e-8, with or without diagonal preconditioning (OSQP, which the reference
+    compares against, is not installed: an exact KKT solve on the identified active set,
+    checked for feasibility and multiplier signs, stands in for it)."""
+    eq_rows, in_rows, data, matrix = coupled_diagonal_qp_case()
+    cfg = ChambollePockConfig(tolerance=1e-9, max_iterations=20000, row_scaling=False,
+                              diagonal_preconditioning=diagonal)
+    result, _ = OracleDiagonalQP(6, eq_rows, in_rows, oracle_config(cfg)).solve(data)
+    assert (result["status"] == 0).all()
+    q, c, _, rhs, lower, upper = data
+    for i in range(len(q)):
+        exact = kkt_certified_qp(q[i], c[i], matrix, rhs[i], 2, lower[i], upper[i], result["y"][i])
+        np.testing.assert_allclose(result["y"][i], exact, atol=3e-8)
