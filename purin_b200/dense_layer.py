@@ -36,6 +36,7 @@ gradient, where BiCGSTAB's last iterate would be returned.
 from __future__ import annotations
 
 import contextlib
+from numbers import Integral
 
 import numpy as np
 import torch
@@ -116,13 +117,20 @@ def ruiz_equilibrate(q, c, A, b, C, d, lower, upper, *, iterations=4, eps=1e-6):
 
 
 def inequality_rows(inequality_support, mi, n):
-    """Column supports of the inequality rows: full rows, or the packed support."""
+    """Column supports of the inequality rows: full rows, or the packed support,
+    validated as ``sparse_layer.py:24-44`` does (one row per inequality; integer
+    indices in [0, n), booleans excluded; no duplicates within a row)."""
     if inequality_support is None:
         return tuple(tuple(range(n)) for _ in range(mi))
-    rows = tuple(tuple(int(i) for i in row) for row in inequality_support)
+    rows = tuple(tuple(row) for row in inequality_support)
     if len(rows) != mi:
-        raise ValueError("inequality_support must have one row per inequality")
-    return rows
+        raise ValueError("inequality_support must have one row per inequality.")
+    for row in rows:
+        if any(not isinstance(i, Integral) or isinstance(i, bool) or i < 0 or i >= n for i in row):
+            raise ValueError("Sparse support indices must be integers in [0, n).")
+        if len(set(row)) != len(row):
+            raise ValueError("Sparse support rows cannot contain duplicate indices.")
+    return tuple(tuple(int(i) for i in row) for row in rows)
 
 
 class _DenseSolver:

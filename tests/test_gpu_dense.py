@@ -247,3 +247,101 @@ def test_qp_forward_resume_is_bitwise_uninterrupted(accelerated):
     for key in ("y", "ybar", "dual"):
         assert torch.equal(resumed[key], whole[key]), key
     assert resumed["iterations"].tolist() == [trips] * 4 == whole["iterations"].tolist()
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+@pytest.mark.parametrize("support", [None, ((0,),)])
+@pytest.mark.parametrize("equilibrate", [False, True])
+def test_iteration_counts_preserve_solution(accelerated, support, equilibrate):
+    """PURIN tests/test_cp_iteration_counts.py:10-43: asking for the counts changes no
+    output; the batch advances every row until the shared loop exits (8, 8), and the
+    first sample alone is accepted after one iteration."""
+    t = lambda x: torch.as_tensor(np.asarray(x, dtype=np.float64), device=DEV)
+    arguments = (t(np.ones((2, 1))), t([[0.0], [-2.0]]), t(np.empty((0, 1))), t(np.empty((0,))),
+                 t(np.ones((1, 1))), t(np.ones((1,))), t([-np.inf]), t([np.inf]))
+    options = dict(accelerated=accelerated, inequality_support=support,
+                   equilibrate=equilibrate, max_iterations=8, tolerance=1e-12)
+    expected = solve_dense_implicit(*arguments, **options)
+    *actual, iterations = solve_dense_implicit(*arguments, **options, return_iterations=True)
+    for result, reference in zip(actual, expected):
+        np.testing.assert_allclose(result.cpu().numpy(), reference.cpu().numpy(), atol=1e-12,
+                                   rtol=1e-12)
+    assert iterations.cpu().tolist() == [8, 8]
+    singleton = tuple(value[:1] if i < 2 else value for i, value in enumerate(arguments))
+    *_, early = solve_dense_implicit(*singleton, **options, return_iterations=True)
+    assert early.cpu().tolist() == [1]
+
+
+@pytest.mark.parametrize("accelerated", [False, True])
+@pytest.mark.parametrize("equilibrate", [False, True])
+@pytest.mark.parametrize("concentrated", [False, True])
+def test_sparse_forward_and_structural_gradients(accelerated, equilibrate, concentrated):
+    """PURIN tests/test_sparse_cp_layer.py:11-71: the packed support (an empty row
+    included; or every row on the same two columns) gives the dense layout's outputs
+    and gradients of every input to the adjoint's accuracy."""
+    rng = np.random.default_rng(7)
+    n, me, mi, batch = 8, 2, 3, 2
+    rows = ((0, 2), (), (1, 4, 7))
+    if concentrated:
+        n = 32
+        rows = ((0, 1),) * mi
+    mask = np.zeros((mi, n))
+    for i, row in enumerate(rows):
+        mask[i, list(row)] = 1
+    t = lambda x: torch.as_tensor(np.asarray(x, dtype=np.float64), device=DEV)
+    q = t(rng.uniform(1, 2, (batch, n)))
+    c = t(rng.normal(size=(batch, n)))
+    a = t(rng.normal(size=(batch, me, n)))
+    b = t(np.zeros((batch, me)))
+    matrix = t(rng.normal(size=(batch, mi, n)))
+    d = t(np.tile([0.05, 1, 0.05], (batch, 1)))
+    lower, upper = -torch.ones_like(q), torch.ones_like(q)
+    masked = matrix * t(mask)
+    outputs, grads = [], []
+    for sparse in (False, True):
+        params = [x.clone().requires_grad_(True) for x in (q, c, a, b, masked, d, lower, upper)]
+        out = solve_dense_implicit(*params, accelerated=accelerated, equilibrate=equilibrate,
+                                   max_iterations=500, norm_iterations=25,
+                                   inequality_support=rows if sparse else None)
+        outputs.append([o.detach().cpu().numpy() for o in out])
+        weights = [torch.as_tensor(np.random.default_rng(11 + k).normal(size=tuple(o.shape)),
+                                   device=DEV) for k, o in enumerate(out)]
+        sum((w * o).sum() for w, o in zip(weights, out)).backward()
+        grads.append([np.zeros(tuple(p.shape)) if p.grad is None else p.grad.cpu().numpy()
+                      for p in params])
+    for x, y in zip(*outputs):
+        np.testing.assert_allclose(x, y, atol=2e-7, rtol=2e-6)
+    for k, (x, y) in enumerate(zip(*grads)):
+        if k == 4:  # the matrix: only its structural entries are shared by both layouts
+            x, y = x * mask, y * mask
+        np.testing.assert_allclose(x, y, atol=5e-6, rtol=2e-5)
+        assert np.linalg.norm(x - y) <= 1e-5 * max(1.0, np.linalg.norm(x))
+
+
+@pytest.mark.parametrize("rows", [((0,),), ((0,), (8,)), ((0,), (1, 1)), ((0,), (0.5,)),
+                                  ((0,), (True,))])
+def test_invalid_support_rejected(rows):
+    """PURIN tests/test_sparse_cp_layer.py:74-81 (and booleans, which the reference's
+    validation also excludes)."""
+    q = torch.ones((1, 8), dtype=torch.float64, device=DEV)
+    empty = torch.zeros((1, 0, 8), dtype=torch.float64, device=DEV)
+    C = torch.ones((1, 2, 8), dtype=torch.float64, device=DEV)
+    with pytest.raises(ValueError):
+        solve_dense_implicit(q, q, empty, torch.zeros((1, 0), device=DEV, dtype=torch.float64),
+                             C, torch.ones((1, 2), dtype=torch.float64, device=DEV), -q, q,
+                             inequality_support=rows)
+
+
+def test_zero_constraint_blocks_with_packed_support():
+    """PURIN tests/test_sparse_cp_layer.py:84-122: no rows, packed support () against the
+    dense call."""
+    t = lambda x: torch.as_tensor(np.asarray(x, dtype=np.float64), device=DEV)
+    q, c = t([[1.0, 2.0, 3.0]]), t([[0.2, -0.6, 0.9]])
+    empty, rhs = t(np.zeros((1, 0, 3))), t(np.zeros((1, 0)))
+    y, eq, iq = solve_dense_implicit(q, c, empty, rhs, empty, rhs, -torch.ones_like(q),
+                                     torch.ones_like(q), inequality_support=(),
+                                     max_iterations=500)
+    dense = solve_dense_implicit(q, c, empty, rhs, empty, rhs, -torch.ones_like(q),
+                                 torch.ones_like(q), max_iterations=500)
+    np.testing.assert_allclose(y.cpu().numpy(), dense[0].cpu().numpy(), atol=1e-12)
+    assert tuple(eq.shape) == tuple(iq.shape) == (1, 0)
