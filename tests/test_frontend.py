@@ -105,11 +105,17 @@ def test_config_validation(kwargs, match):
         ChambollePockConfig(**kwargs)
 
 
-def test_linear_and_gradient_config_validation():
+@pytest.mark.parametrize("factory,kwargs", [
+    (LinearSolverConfig, dict(tolerance=0)), (LinearSolverConfig, dict(atol=-1)),
+    (LinearSolverConfig, dict(restart=0)), (LinearSolverConfig, dict(max_iterations=0)),
+    (ImplicitGradientConfig, dict(policy="bad")),
+    (ImplicitGradientConfig, dict(invalid_batch_policy="bad")),
+    (ImplicitGradientConfig, dict(inexact_tolerance=-1)),
+    (ImplicitGradientConfig, dict(adjoint_tolerance=-1))])
+def test_linear_and_gradient_config_validation(factory, kwargs):
+    """PURIN tests/test_validation.py:29-37 (the CP path's configuration classes)."""
     with pytest.raises(ValueError):
-        LinearSolverConfig(restart=0)
-    with pytest.raises(ValueError):
-        ImplicitGradientConfig(policy="bogus")
+        factory(**kwargs)
     assert ChambollePockConfig().linear_solver.restart == 30
 
 
