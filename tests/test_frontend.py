@@ -105,6 +105,14 @@ def test_config_validation(kwargs, match):
         ChambollePockConfig(**kwargs)
 
 
+@pytest.mark.parametrize("bad", [[], [0.0], [np.inf], [[1.0]]])
+def test_metric_diagonal_validation(bad):
+    """PURIN tests/test_linear_algebra.py:153-156 (validate_metric_diagonal)."""
+    with pytest.raises(ValueError):
+        ChambollePockConfig(metric_diagonal=bad)
+    assert ChambollePockConfig(metric_diagonal=[1.0, 2.0]).metric_diagonal == (1.0, 2.0)
+
+
 @pytest.mark.parametrize("factory,kwargs", [
     (LinearSolverConfig, dict(tolerance=0)), (LinearSolverConfig, dict(atol=-1)),
     (LinearSolverConfig, dict(restart=0)), (LinearSolverConfig, dict(max_iterations=0)),
