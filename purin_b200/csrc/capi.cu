@@ -143,6 +143,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   int best = -1;
   int64_t best_warps = -1, best_samples = -1;
   int pair_blocks = 0;  // resident CTAs per SM of the two-sample 256-thread tile (shape 1)
+  int quad_blocks = 0;  // ... and of the four-sample one (shape 2)
   for (int k = 0; k < kForwardShapeCount; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
     if (qp && S != 1) continue;  // the QP kernels are built for one-sample tiles
@@ -166,6 +167,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
                    : purin::forward_blocks_per_sm<float>(S, NT, shared_values, dyn, qp);
     }
     if (k == 1) pair_blocks = std::max(cached, 0);
+    if (k == 2) quad_blocks = std::max(cached, 0);
     const int64_t tiles = (batch + S - 1) / S;
     const int64_t ctas = std::min<int64_t>(tiles, sms * std::max(cached, 0));
     const int64_t warps = ctas * (NT / 32);
@@ -185,6 +187,18 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   if (!f64 && best >= 0 && forced == 0 && forced_threads == 0 && pair_blocks >= 2 &&
       (batch + 1) / 2 >= sms * pair_blocks && kShapes[best][0] == 1)
     best = 1;
+  // fp32 four-sample tiles with three CTAs per SM share each structure load and
+  // each gather instruction among four samples; a tile takes about 1.27x a
+  // two-sample tile's time (configuration 1 fp32: 11.4 against 9.0 ms per wave),
+  // so per sample they are faster when whole waves are compared.  Chosen when
+  // their waves, weighted by that ratio, beat the two-sample tiles' waves:
+  // 4096 samples 108.3k -> 113.2k samples/s (3 waves against 4); at 2048 the
+  // two-sample tiles stay (2 waves each).
+  if (!f64 && best == 1 && quad_blocks >= 3 && pair_blocks >= 1) {
+    const int64_t pair_waves = ((batch + 1) / 2 + sms * pair_blocks - 1) / (sms * pair_blocks);
+    const int64_t quad_waves = ((batch + 3) / 4 + sms * quad_blocks - 1) / (sms * quad_blocks);
+    if (127 * quad_waves < 100 * pair_waves) best = 2;
+  }
   // A structure far larger than the L1 beside the tile state streams from L2
   // once per tile-iteration (value plus 16-bit index per stored entry, both
   // products).  A wide tile of 4 (else 2) samples on 768 threads shares that
