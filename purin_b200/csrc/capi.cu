@@ -142,7 +142,8 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   const bool narrow_ok = qp && (int64_t)n_pos + m_pos <= 4 * purin::kNarrowThreads;
   int best = -1;
   int64_t best_warps = -1, best_samples = -1;
-  int pair_blocks = 0;  // resident CTAs per SM of the two-sample 256-thread tile (shape 1)
+  int single_blocks = 0;  // resident CTAs per SM of the one-sample 256-thread tile (shape 0)
+  int pair_blocks = 0;  // ... of the two-sample one (shape 1)
   int quad_blocks = 0;  // ... and of the four-sample one (shape 2)
   for (int k = 0; k < kForwardShapeCount; ++k) {
     const int S = kShapes[k][0], NT = kShapes[k][1];
@@ -166,6 +167,7 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
       cached = f64 ? purin::forward_blocks_per_sm<double>(S, NT, shared_values, dyn, qp)
                    : purin::forward_blocks_per_sm<float>(S, NT, shared_values, dyn, qp);
     }
+    if (k == 0) single_blocks = std::max(cached, 0);
     if (k == 1) pair_blocks = std::max(cached, 0);
     if (k == 2) quad_blocks = std::max(cached, 0);
     const int64_t tiles = (batch + S - 1) / S;
@@ -187,6 +189,19 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   if (!f64 && best >= 0 && forced == 0 && forced_threads == 0 && pair_blocks >= 2 &&
       (batch + 1) / 2 >= sms * pair_blocks && kShapes[best][0] == 1)
     best = 1;
+  // fp64 two-sample tiles with three CTAs per SM (80 registers) share each
+  // structure load between two samples; a tile takes about 1.25x a one-sample
+  // tile's time (configuration 1 fp64: 11.5 against 9.2 ms per wave), so they are
+  // taken when their waves, weighted by that ratio, beat the one-sample tiles'
+  // waves: configuration 1 fp64 at 4096 samples 59.3k -> 67.9k samples/s, at
+  // 16 384 62.4k -> 73.3k.  Configuration 2's samples (45 KB) leave room for two
+  // such tiles per SM only, and keep the one-sample tiles.
+  if (f64 && best == 0 && forced == 0 && forced_threads == 0 && pair_blocks >= 3 &&
+      single_blocks >= 1) {
+    const int64_t single_waves = (batch + sms * single_blocks - 1) / (sms * single_blocks);
+    const int64_t pair_waves = ((batch + 1) / 2 + sms * pair_blocks - 1) / (sms * pair_blocks);
+    if (125 * pair_waves < 100 * single_waves) best = 1;
+  }
   // fp32 four-sample tiles with three CTAs per SM share each structure load and
   // each gather instruction among four samples; a tile takes about 1.27x a
   // two-sample tile's time (configuration 1 fp32: 11.4 against 9.0 ms per wave),

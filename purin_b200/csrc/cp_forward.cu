@@ -252,15 +252,16 @@ __device__ __forceinline__ T dual_minimiser(T tt, T qj, T l, T u) {
 // thread for one-sample tiles): 1 x 1024 or 768, 2 x 512 (one CTA of 512 for
 // wider tiles, 128 registers), 8 x 128, or 4 / 2 / 1 CTAs of 256 threads for
 // S = 1 / 2 / wider.  fp32 two-sample tiles also fit 64 registers (no spills;
-// 87 unconstrained), so they keep 4 CTAs per SM like the one-sample tiles, and
-// fp32 four-sample tiles fit 80 registers (3 CTAs per SM; 141 unconstrained).
+// 87 unconstrained), so they keep 4 CTAs per SM like the one-sample tiles;
+// fp64 two-sample and fp32 four-sample tiles fit 80 registers (3 CTAs per SM;
+// 122 and 141 unconstrained, a 4-byte spill).
 constexpr int forward_min_blocks(int S, int NT, int elem_bytes) {
   return NT >= 1024                    ? 1
          : NT >= 512                   ? (S == 1 ? 2 : 1)
          : NT <= 128                   ? 8
          : S == 1                      ? 4
          : (S == 2 && elem_bytes == 4) ? 4
-         : S == 2                      ? 2
+         : S == 2                      ? 3
          : (S == 4 && elem_bytes == 4) ? 3
                                        : 1;
 }
