@@ -148,3 +148,18 @@ def test_layout_helpers():
     row_ptr = np.array([0, 2, 2, 5])
     np.testing.assert_array_equal(ell_index(row_ptr), [[0, 1, 5], [5, 5, 5], [2, 3, 4]])
     np.testing.assert_array_equal(rows_of(row_ptr), [0, 0, 2, 2, 2])
+
+
+@pytest.mark.parametrize("rows", [((0,),), ((0,), (8,)), ((0,), (-1,)), ((0,), (1, 1)),
+                                  ((0,), (0.5,)), ((0,), (True,))])
+def test_packed_support_validation(rows):
+    """The dense adapter's packed supports are validated as sparse_layer.py:24-44 does."""
+    from purin_b200.dense_layer import inequality_rows
+    with pytest.raises(ValueError):
+        inequality_rows(rows, 2, 8)
+
+
+def test_packed_support_accepts_numpy_integers_and_empty_rows():
+    from purin_b200.dense_layer import inequality_rows
+    assert inequality_rows(((np.int64(0), 3), ()), 2, 8) == ((0, 3), ())
+    assert inequality_rows(None, 2, 3) == ((0, 1, 2), (0, 1, 2))
