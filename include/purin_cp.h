@@ -248,7 +248,9 @@ int32_t purin_cp_workspace_size(const PurinCpPlan* plan, int32_t op, int64_t bat
  * purin_cp_forward call of `batch` samples runs on this plan -- samples per
  * CTA, threads per CTA, and 1 when the tile state lives in shared memory (0:
  * in the workspace).  shared_values: 1 when the call's values are shared by
- * the batch.  Tile shapes differ only in speed, never in results. */
+ * the batch.  Tile shapes differ only in speed, never in results.
+ * purin_qp_forward always runs one-sample tiles; this reports the shape of a
+ * purin_cp_forward call. */
 int32_t purin_cp_forward_shape(const PurinCpPlan* plan, const PurinCpConfig* config, int64_t batch,
                                int32_t shared_values, int32_t* samples_per_tile, int32_t* threads,
                                int32_t* shared_state);
