@@ -209,7 +209,8 @@ FwdPlan plan_forward_tiles(PurinCpPlan* plan, const PurinCpConfig* cfg, int64_t 
   // their waves, weighted by that ratio, beat the two-sample tiles' waves:
   // 4096 samples 108.3k -> 113.2k samples/s (3 waves against 4); at 2048 the
   // two-sample tiles stay (2 waves each).
-  if (!f64 && best == 1 && quad_blocks >= 3 && pair_blocks >= 1) {
+  if (!f64 && best == 1 && forced == 0 && forced_threads == 0 && quad_blocks >= 3 &&
+      pair_blocks >= 1) {
     const int64_t pair_waves = ((batch + 1) / 2 + sms * pair_blocks - 1) / (sms * pair_blocks);
     const int64_t quad_waves = ((batch + 3) / 4 + sms * quad_blocks - 1) / (sms * quad_blocks);
     if (127 * quad_waves < 100 * pair_waves) best = 2;
